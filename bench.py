@@ -1,0 +1,455 @@
+"""Benchmark of the Newton-Schulz / Muon hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload ns|muon1b|muon8b]
+                    [--impl ours|reference]
+
+Workloads:
+  ns      configs[1] headline: 5-step Newton-Schulz on one (4096, 4096) bf16
+          N(0,1) matrix (seed 0).  One step = one fused_newton_schulz call.
+          Default at N = 1.  L2 (126 MB) is flushed with a 256 MB write before
+          every timed step (outside the step's events).
+  muon1b  configs[3]: FusedMuon.step() over the 112 matrices of the 1B-class
+          Llama shape set, grads N(0, 1e-3), lr 0.02, momentum 0.95, nesterov.
+  muon8b  configs[4]: the same over the 224 matrices of the 8B-class set,
+          matrices sharded across the N ranks (FLOP-balanced) with an NCCL
+          all-gather of the bf16 updates.  Default at N > 1.
+
+The metric is dense-equivalent Newton-Schulz TFLOP/s (the reference's count,
+5·(4m²n + 2m³) per matrix; docs/optimization_report.md:24-29), whole job, max
+over ranks; µs per NS / ms per step are reported beside it.
+
+--impl reference times the reference's own algorithm on the host CPU cores
+(the oracle's op-for-op restatement of muon_fused/ns_step.py:25-55, since the
+reference's path is pure PyTorch and is not installed on the GPU box), on a
+bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+NS_STEPS = 5
+SHAPE_NS = (4096, 4096)
+
+
+def ns_flops(m: int, n: int, steps: int = NS_STEPS) -> float:
+    m, n = min(m, n), max(m, n)
+    return steps * (4.0 * m * m * n + 2.0 * m ** 3)
+
+
+def llama_shapes(kind: str):
+    """Per-layer Muon matrices of the 1B / 8B Llama-style sets."""
+    if kind == "muon1b":
+        h, kv, ffn, layers = 2048, 512, 8192, 16
+    else:
+        h, kv, ffn, layers = 4096, 1024, 14336, 32
+    per_layer = [(h, h), (kv, h), (kv, h), (h, h), (ffn, h), (ffn, h), (h, ffn)]  # q k v o gate up down
+    return [s for _ in range(layers) for s in per_layer]
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d, "measured"
+    return PEAKS_FALLBACK, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        sm, smax, reasons = [], 0.0, set()
+        for l in getattr(self, "lines", []):
+            f = [x.strip() for x in l.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = max(smax, float(f[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# --------------------------------------------------------------------------- helpers
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def barrier_max(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def flush_l2(buf: torch.Tensor) -> None:
+    buf.fill_(1)
+
+
+def torch_eager_ns(G: torch.Tensor, steps: int) -> torch.Tensor:
+    """The reference's pure-PyTorch NS (muon_fused/ns_step.py:25-55) on the GPU:
+    the path a reference user gets on B200, where its sm_80 extension is not
+    built.  Reported beside our number, not used as an oracle."""
+    a, b, c = 3.4445, -4.7750, 2.0315
+    X = G.bfloat16()
+    if G.size(0) > G.size(1):
+        X = X.T
+    X = X / (X.norm() + 1e-7)
+    for _ in range(steps):
+        A = X @ X.T
+        B = b * A + c * A @ A
+        X = a * X + B @ X
+    if G.size(0) > G.size(1):
+        X = X.T
+    return X
+
+
+# --------------------------------------------------------------------------- CPU arms
+def cpu_ns_sample(budget_s: float):
+    """Time the reference's algorithm (oracle restatement) on host cores on the
+    headline matrix; returns (TFLOP/s, seconds per call, calls, threads)."""
+    from oracle import ns_oracle as O
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    G = torch.randn(*SHAPE_NS, generator=torch.Generator().manual_seed(0)).bfloat16()
+    O.ns_reference_bf16(G[:512, :512], NS_STEPS)  # warm the BLAS
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while True:
+        t0 = time.perf_counter()
+        O.ns_reference_bf16(G, NS_STEPS)
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() > t_end or len(times) >= 5:
+            break
+    med = statistics.median(times)
+    return ns_flops(*SHAPE_NS) / med / 1e12, med, len(times), threads
+
+
+def run_reference_arm(args, world, rank):
+    if rank != 0:
+        return
+    from oracle import ns_oracle as O
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    wl = args.workload
+    if wl == "ns":
+        G = torch.randn(*SHAPE_NS, generator=torch.Generator().manual_seed(0)).bfloat16()
+        unit_flops, sample = ns_flops(*SHAPE_NS), "one 5-step NS on (4096,4096) per step"
+        fn = lambda: O.ns_reference_bf16(G, NS_STEPS)
+    else:
+        # one layer of the set (7 matrices) per step; the metric is a rate, so
+        # the per-layer rate stands for the whole step
+        shapes = llama_shapes(wl)[:7]
+        gs = [torch.randn(s, generator=torch.Generator().manual_seed(1000 + i)) * 1e-3
+              for i, s in enumerate(shapes)]
+        unit_flops = sum(ns_flops(*s) for s in shapes)
+        sample = f"one layer ({len(shapes)} matrices) of the {wl} set per step, NS only"
+        fn = lambda: [O.ns_reference_bf16(g, NS_STEPS) for g in gs]
+    for _ in range(args.warmup):
+        fn()
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        fn()
+        times.append(time.perf_counter() - t0)
+    t = statistics.mean(times)
+    value = unit_flops / t / 1e12
+    line = {
+        "impl": "reference", "metric": metric_name(wl), "value": round(value, 4),
+        "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(t * 1e3, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": config_for(wl, world),
+        "cpu_baseline": {"value": round(value, 4), "unit": "TFLOP/s", "cores": threads,
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def metric_name(wl: str) -> str:
+    if wl == "ns":
+        return "5-step Newton-Schulz dense-equivalent TFLOP/s, (4096,4096) bf16"
+    return f"FusedMuon.step Newton-Schulz dense-equivalent TFLOP/s, {wl} shape set"
+
+
+def config_for(wl: str, world: int):
+    if wl == "ns":
+        return {"workload": "ns_5step_4096x4096", "shape": list(SHAPE_NS), "ns_steps": NS_STEPS,
+                "seed": 0, "l2": "flushed (256 MB write) before every timed step",
+                "parallelism": "replicas" if world > 1 else "single"}
+    shapes = llama_shapes(wl)
+    return {"workload": f"fusedmuon_step_{wl}", "matrices": len(shapes), "ns_steps": NS_STEPS,
+            "lr": 0.02, "momentum": 0.95, "nesterov": True,
+            "l2": "working set (params+grads+momentum) far above L2",
+            "parallelism": f"matrix-sharded dp{world}" if world > 1 else "single"}
+
+
+# --------------------------------------------------------------------------- our arm
+def bench_ns(args, peaks, peak_src):
+    from muon_fused import _lib, fused_newton_schulz, workspace_size
+
+    dev = torch.device("cuda")
+    m, n = SHAPE_NS
+    G = torch.randn(m, n, generator=torch.Generator(device=dev).manual_seed(0), device=dev,
+                    dtype=torch.bfloat16)
+    ws = torch.empty(workspace_size(m, n), dtype=torch.uint8, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        fused_newton_schulz(G, NS_STEPS, ws)
+    torch.cuda.synchronize()
+
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        for s, e in evs:
+            flush_l2(flush)
+            s.record(stream)
+            fused_newton_schulz(G, NS_STEPS, ws)
+            e.record(stream)
+        torch.cuda.synchronize()
+    t_ms = [s.elapsed_time(e) for s, e in evs]
+    ms = statistics.mean(t_ms)
+    flops = ns_flops(m, n)
+
+    # per-kernel timing pass (events around every launch, same stream)
+    _lib.stage_timing(True)
+    for _ in range(args.steps):
+        flush_l2(flush)
+        fused_newton_schulz(G, NS_STEPS, ws)
+    st = _lib.stage_times()
+    _lib.stage_timing(False)
+    stage_flops = {"gemm1_syrk": 2.0 * m * m * n, "gemm2_poly": 2.0 * m ** 3,
+                   "gemm3_bx": 2.0 * m * m * n}
+    stages = {}
+    for k, (tot, cnt) in st.items():
+        if cnt:
+            avg = tot / cnt
+            d = {"launches": cnt, "avg_us": round(avg * 1e3, 2),
+                 "share": round(tot / sum(v[0] for v in st.values()), 4)}
+            if k in stage_flops:
+                d["dense_eq_tflops"] = round(stage_flops[k] / (avg * 1e-3) / 1e12, 1)
+            stages[k] = d
+    dom = "gemm3_bx"
+    avg_dom = st[dom][0] / st[dom][1]
+    achieved = stage_flops[dom] / (avg_dom * 1e-3) / 1e12
+    peak = float(peaks["bf16_tflops"])
+    roofline = {"bound": "tensor", "kernel": "ns_gemm_kernel<kBX> (X' = d*X + Boff*X)",
+                "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
+                "frac": round(achieved / peak, 4), "peak_source": f"{peak_src} bf16_tflops (burst)",
+                "traffic": None, "stages": stages}
+
+    # end to end: pinned host G -> device -> NS -> pinned host result
+    G_host = G.cpu().pin_memory()
+    out_host = torch.empty((m, n), dtype=torch.bfloat16).pin_memory()
+    G_dev = torch.empty_like(G)
+    for _ in range(2):
+        G_dev.copy_(G_host, non_blocking=True)
+        out_host.copy_(fused_newton_schulz(G_dev, NS_STEPS, ws), non_blocking=True)
+    torch.cuda.synchronize()
+    evs2 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            for _ in range(args.steps)]
+    for s, e in evs2:
+        flush_l2(flush)
+        s.record(stream)
+        G_dev.copy_(G_host, non_blocking=True)
+        out_host.copy_(fused_newton_schulz(G_dev, NS_STEPS, ws), non_blocking=True)
+        e.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = statistics.mean(s.elapsed_time(e) for s, e in evs2)
+
+    # the reference's PyTorch path on this GPU (what a reference user runs on B200)
+    for _ in range(3):
+        torch_eager_ns(G, NS_STEPS)
+    torch.cuda.synchronize()
+    evs3 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            for _ in range(args.steps)]
+    for s, e in evs3:
+        flush_l2(flush)
+        s.record(stream)
+        torch_eager_ns(G, NS_STEPS)
+        e.record(stream)
+    torch.cuda.synchronize()
+    eager_ms = statistics.mean(s.elapsed_time(e) for s, e in evs3)
+
+    return {
+        "ms": ms, "flops": flops, "t_ms": t_ms, "roofline": roofline, "clocks": clk.summary(),
+        "e2e": {"value": round(flops / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+                "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": G_host.nbytes,
+                "d2h_bytes_per_step": out_host.nbytes},
+        "launches": args.steps * (2 + 3 * NS_STEPS),
+        "extra": {"us_per_ns": round(ms * 1e3, 1),
+                  "useful_tflops": round(NS_STEPS * (m * (m + 1) * n + m * m * (m + 1)
+                                                     + 2.0 * m * m * n) / (ms * 1e-3) / 1e12, 1),
+                  "torch_eager_gpu_ms": round(eager_ms, 4),
+                  "speedup_vs_torch_eager_gpu": round(eager_ms / ms, 3)},
+    }
+
+
+def bench_muon(args, world, rank, peaks, peak_src):
+    from muon_fused import FusedMuon, _lib
+
+    dev = torch.device("cuda")
+    shapes = llama_shapes(args.workload)
+    params = []
+    for i, s in enumerate(shapes):
+        g = torch.Generator(device=dev).manual_seed(i)
+        p = torch.nn.Parameter(torch.randn(s, generator=g, device=dev, dtype=torch.bfloat16) * 0.02)
+        p.grad = torch.randn(s, generator=torch.Generator(device=dev).manual_seed(1000 + i),
+                             device=dev, dtype=torch.bfloat16) * 1e-3
+        params.append(p)
+    opt = FusedMuon([{"params": params, "use_muon": True}], lr=0.02, momentum=0.95, nesterov=True,
+                    ns_steps=NS_STEPS)
+    for _ in range(args.warmup):
+        opt.step()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+    torch.cuda.synchronize()
+    s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        s_ev.record(stream)
+        for _ in range(args.steps):
+            opt.step()
+        e_ev.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+    ms = s_ev.elapsed_time(e_ev) / args.steps
+    ms = barrier_max(ms, world)
+    flops = sum(ns_flops(*s) for s in shapes)
+    return {"ms": ms, "flops": flops, "roofline": None, "clocks": clk.summary(), "e2e": None,
+            "launches": None, "extra": {"matrices": len(shapes)}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", choices=["ns", "muon1b", "muon8b"], default=None)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-budget", type=float, default=15.0,
+                    help="seconds of host-CPU baseline sampling (rank 0, N=1)")
+    args = ap.parse_args()
+    world, rank, local = dist_env()
+    if args.workload is None:
+        args.workload = "ns" if world == 1 else "muon8b"
+    args.warmup = max(args.warmup, 3)
+
+    if args.impl == "reference":
+        run_reference_arm(args, world, rank)
+        return
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    peaks, peak_src = load_peaks()
+    if args.workload == "ns":
+        r = bench_ns(args, peaks, peak_src)
+        r["ms"] = barrier_max(r["ms"], world)
+        value = world * r["flops"] / (r["ms"] * 1e-3) / 1e12
+    else:
+        r = bench_muon(args, world, rank, peaks, peak_src)
+        value = r["flops"] / (r["ms"] * 1e-3) / 1e12
+
+    if rank == 0:
+        line = {
+            "metric": metric_name(args.workload), "value": round(value, 2), "unit": "TFLOP/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(r["ms"], 4), "higher_is_better": True,
+            "scaling": "weak" if args.workload == "ns" else "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": config_for(args.workload, world),
+            "clocks": r["clocks"], "gpu_launches": r["launches"],
+        }
+        if r["e2e"] is not None:
+            line["e2e"] = r["e2e"]
+        if r["roofline"] is not None:
+            line["roofline"] = r["roofline"]
+        line.update(r["extra"])
+        if world == 1 and args.workload == "ns":
+            v, sec, calls, threads = cpu_ns_sample(args.cpu_budget)
+            line["cpu_baseline"] = {"value": round(v, 4), "unit": "TFLOP/s", "cores": threads,
+                                    "kind": "port",
+                                    "sample": f"{calls} x 5-step NS on (4096,4096), median {sec:.2f} s"}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,113 @@
+/*
+ * fused_muon.h — C ABI of the B200 (sm_100a) Newton-Schulz engine.
+ *
+ * Plain pointers, sizes and a CUDA stream handle (passed as void*); no torch
+ * or C++ types cross this boundary.  Every call is asynchronous on `stream`
+ * and returns 0 on success or a negative FM_E* code; fm_last_error() gives a
+ * message for the calling thread's last failure.  Device pointers must be
+ * on the current CUDA device.
+ *
+ * Each entry point names the reference interface it replaces
+ * (StarrickLiu/fused-muon).
+ */
+#ifndef FUSED_MUON_H_
+#define FUSED_MUON_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+#define FM_OK 0
+#define FM_E_INVALID (-1)   /* bad argument (shape, pointer, dtype, size) */
+#define FM_E_WORKSPACE (-2) /* workspace smaller than fm_workspace_size() */
+#define FM_E_CUDA (-3)      /* CUDA runtime / driver error */
+#define FM_E_DEVICE (-4)    /* unsupported device (needs sm_100) */
+
+/* Input element types accepted by fm_fused_newton_schulz (output is bf16). */
+#define FM_DT_BF16 0
+#define FM_DT_F16 1
+#define FM_DT_F32 2
+#define FM_DT_F64 3
+
+/* Library version, e.g. 100 for 0.1.0. */
+int fm_version(void);
+
+/* Message for the calling thread's most recent failed call ("" if none). */
+const char* fm_last_error(void);
+
+/*
+ * Workspace bytes needed by fm_fused_newton_schulz / fm_newton_schulz_step for
+ * a rows x cols matrix (either orientation).
+ * Replaces: csrc/ns_gemm.cu:37-52 newton_schulz_workspace_size(m, n) and
+ * csrc/torch_binding.cu:16-18 query_workspace_size (exported as
+ * _C.workspace_size, torch_binding.cu:132-134).
+ */
+int fm_workspace_size(int64_t rows, int64_t cols, uint64_t* bytes);
+
+/*
+ * Full Newton-Schulz orthogonalisation: out = NS_steps(G) in bf16.
+ * G: rows x cols, row stride ldg (elements), element type `dtype`.
+ * out: rows x cols bf16, contiguous.  Tall inputs (rows > cols) are handled
+ * by working on Gᵀ and writing the result back transposed.
+ * workspace: device buffer of at least fm_workspace_size(rows, cols) bytes,
+ * 256-byte aligned.
+ * Replaces: csrc/torch_binding.cu:58-123 fused_newton_schulz (pybind
+ * _C.fused_newton_schulz) and the Python front muon_fused/ns_step.py:85-123.
+ */
+int fm_fused_newton_schulz(const void* G, int dtype, int64_t rows, int64_t cols, int64_t ldg,
+                           void* out, int steps, void* workspace, uint64_t workspace_bytes,
+                           void* stream);
+
+/*
+ * One Newton-Schulz iteration on an already normalised bf16 matrix:
+ * X_new = (a·I + b·A + c·A²)·X with A = X·Xᵀ.  X: m x n bf16 with row stride
+ * ldx; X_new: m x n bf16, contiguous.  No transpose is applied.
+ * Replaces: csrc/ns_gemm.h:20-25 xcompute::newton_schulz_step and
+ * csrc/torch_binding.cu:22-54 ns_step (pybind _C.newton_schulz_step).
+ */
+int fm_newton_schulz_step(const void* X, int64_t m, int64_t n, int64_t ldx, void* X_new,
+                          void* workspace, uint64_t workspace_bytes, void* stream);
+
+/*
+ * Debug form of one iteration that also returns the intermediates:
+ * A = X·Xᵀ (m x m bf16), Boff = off-diagonal part of b·A + c·A² (m x m bf16,
+ * zero diagonal), diag = a + diagonal of b·A + c·A² (m floats), X_new as in
+ * fm_newton_schulz_step.  All outputs contiguous.
+ * Replaces: nothing exported by the reference; it exposes the products of the
+ * reference's GEMM1/GEMM2 (csrc/ns_gemm.cu:94-118) for symmetry tests.
+ */
+int fm_ns_step_debug(const void* X, int64_t m, int64_t n, int64_t ldx, void* A, void* Boff,
+                     float* diag, void* X_new, void* workspace, uint64_t workspace_bytes,
+                     void* stream);
+
+/*
+ * Reads and clears the device-side error word of the current device
+ * (synchronises the device).  *code is 0 when no kernel reported a timed-out
+ * pipeline wait since the last call.
+ * Replaces: nothing; the reference checks no kernel status
+ * (csrc/syrk_64.cu:45-49, csrc/ns_gemm.cu:97,127).
+ */
+int fm_device_error(uint32_t* code);
+
+/*
+ * Benchmark instrumentation.  fm_stage_timing(1) makes every later launch of
+ * the calling thread record a CUDA event pair around itself on its stream
+ * (fm_stage_timing(0) stops it; either call discards pending pairs).
+ * fm_stage_times() waits for the recorded events and returns, per stage, the
+ * summed milliseconds and the launch count since the last read:
+ * [0] GEMM1 A = X·Xᵀ, [1] GEMM2 polynomial, [2] GEMM3 X' = B·X, [3] norm/scale.
+ * Replaces: nothing; the reference has no instrumentation
+ * (its timing lives in benchmarks/bench_ns_step.py:53-81).
+ */
+int fm_stage_timing(int enable);
+int fm_stage_times(float* ms, int* counts);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FUSED_MUON_H_ */

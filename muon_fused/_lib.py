@@ -1,0 +1,96 @@
+"""ctypes binding of the C ABI in ``include/fused_muon.h``.
+
+The native library is mandatory: there is no CPU or PyTorch fallback.  If the
+library is missing or cannot be loaded, every entry point raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libfused_muon.so")
+
+# Status codes and dtype codes mirrored from include/fused_muon.h.
+FM_OK = 0
+FM_E_INVALID = -1
+FM_E_WORKSPACE = -2
+FM_E_CUDA = -3
+FM_E_DEVICE = -4
+FM_DT_BF16, FM_DT_F16, FM_DT_F32, FM_DT_F64 = 0, 1, 2, 3
+
+# Every symbol the header declares, with its ctypes signature.
+_c_int, _i64, _u64, _vp = ctypes.c_int, ctypes.c_int64, ctypes.c_uint64, ctypes.c_void_p
+SIGNATURES = {
+    "fm_version": (_c_int, []),
+    "fm_last_error": (ctypes.c_char_p, []),
+    "fm_workspace_size": (_c_int, [_i64, _i64, ctypes.POINTER(_u64)]),
+    "fm_fused_newton_schulz": (_c_int, [_vp, _c_int, _i64, _i64, _i64, _vp, _c_int, _vp, _u64, _vp]),
+    "fm_newton_schulz_step": (_c_int, [_vp, _i64, _i64, _i64, _vp, _vp, _u64, _vp]),
+    "fm_ns_step_debug": (_c_int, [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _u64, _vp]),
+    "fm_device_error": (_c_int, [ctypes.POINTER(ctypes.c_uint32)]),
+    "fm_stage_timing": (_c_int, [_c_int]),
+    "fm_stage_times": (_c_int, [ctypes.POINTER(ctypes.c_float), ctypes.POINTER(_c_int)]),
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+class FusedMuonError(RuntimeError):
+    """A C-ABI call returned a non-zero status."""
+
+
+def load() -> ctypes.CDLL:
+    """Load (once) and return the native library, raising if it is absent."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(LIB_PATH):
+                raise ImportError(
+                    f"{LIB_PATH} is missing; build it with `python -m muon_fused.build` "
+                    "(there is no fallback implementation)")
+            lib = ctypes.CDLL(LIB_PATH)
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = lib
+    return _lib
+
+
+def check(rc: int, what: str) -> None:
+    if rc != FM_OK:
+        msg = load().fm_last_error().decode(errors="replace")
+        raise FusedMuonError(f"{what} failed (status {rc}): {msg}")
+
+
+def workspace_bytes(rows: int, cols: int) -> int:
+    out = ctypes.c_uint64(0)
+    check(load().fm_workspace_size(int(rows), int(cols), ctypes.byref(out)), "fm_workspace_size")
+    return int(out.value)
+
+
+def device_error() -> int:
+    code = ctypes.c_uint32(0)
+    check(load().fm_device_error(ctypes.byref(code)), "fm_device_error")
+    return int(code.value)
+
+
+STAGES = ("gemm1_syrk", "gemm2_poly", "gemm3_bx", "prep")
+
+
+def stage_timing(enable: bool) -> None:
+    check(load().fm_stage_timing(1 if enable else 0), "fm_stage_timing")
+
+
+def stage_times():
+    """{stage: (total ms, launches)} since the last read (see fm_stage_times)."""
+    ms = (ctypes.c_float * 4)()
+    cnt = (ctypes.c_int * 4)()
+    check(load().fm_stage_times(ms, cnt), "fm_stage_times")
+    return {STAGES[i]: (float(ms[i]), int(cnt[i])) for i in range(4)}

@@ -1,0 +1,377 @@
+// Persistent tcgen05/TMEM GEMM for the three contractions of one
+// Newton-Schulz iteration (reference: csrc/ns_gemm.cu:54-135 dispatches the
+// same three products to sm_80 SYRK kernels and cuBLAS).
+//
+//   kSyrk  A  = X·Xᵀ                     lower-triangle tiles, mirrored store
+//                                          (reference csrc/syrk_common.cuh:50-188, mode 0)
+//   kPoly  B  = c·A·A + b·A  (off-diag)  lower-triangle tiles, mirrored store;
+//          d  = a + diag(c·A·A + b·A)     kept in fp32
+//                                          (reference csrc/syrk_common.cuh:147-157, mode 1,
+//                                           which folds a·I into a bf16 B instead)
+//   kBX    X' = d ⊙ X + B·X              full tiles; optional transposed store
+//                                          (reference csrc/ns_gemm.cu:125-134, cuBLAS)
+//
+// Why the diagonal of B lives in fp32: B's diagonal is O(1) while the
+// off-diagonal terms are small, so rounding the diagonal to bf16 dominates the
+// iteration's error.  Keeping it in a separate fp32 vector and applying it in
+// the kBX epilogue (d_i·X_ij in fp32) halves the relative error against an fp32
+// Newton-Schulz.  B itself stays bit-symmetric (zero diagonal, each lower
+// element written to both (r,c) and (c,r)).
+//
+// Structure (one CTA per SM, 6 warps):
+//   warp 0      TMA producer: K-blocks of 64 bf16 (128 B rows, 128B swizzle)
+//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
+//   warps 2..5  epilogue: tcgen05.ld TMEM -> registers -> fused math -> global
+// Tile 128 (M) x 256 (N), kStages-deep smem ring, two TMEM accumulators of 256
+// fp32 columns each so the epilogue of tile t overlaps the mainloop of t+1.
+#pragma once
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cstdint>
+
+#include "fm_ptx.cuh"
+
+namespace fm {
+
+enum GemmMode : int { kSyrk = 0, kPoly = 1, kBX = 2 };
+
+constexpr int kBM = 128;
+constexpr int kBN = 256;
+constexpr int kBK = 64;  // 64 bf16 = 128 bytes = one swizzle row
+constexpr int kStages = 4;
+constexpr int kThreads = 192;
+constexpr int kTileABytes = kBM * kBK * 2;  // 16 KB
+constexpr int kTileBBytes = kBN * kBK * 2;  // 32 KB
+constexpr int kStageBytes = kTileABytes + kTileBBytes;
+constexpr int kTmemCols = 2 * kBN;  // two fp32 accumulators
+constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align slack*/ + 256 /*barriers*/;
+
+// Newton-Schulz quintic coefficients (reference muon_fused/ns_step.py:39).
+constexpr float kNsA = 3.4445f;
+constexpr float kNsB = -4.7750f;
+constexpr float kNsC = 2.0315f;
+
+struct GemmArgs {
+  int M;          // output rows (m)
+  int N;          // output columns: m for kSyrk/kPoly, n for kBX
+  int K;          // reduction length: n for kSyrk, m otherwise
+  int num_tiles;  // scheduled tiles
+  int tiles_n;    // kBX: column tiles per row block
+  __nv_bfloat16* out;
+  long long ld_out;
+  const __nv_bfloat16* aux;  // kPoly: A (for b·A); kBX: X (for d ⊙ X)
+  long long ld_aux;
+  float* diag;        // kPoly: written; kBX: read
+  int transpose_out;  // kBX: store X'ᵀ (ld_out is then the row stride of X'ᵀ)
+  unsigned* err;      // device error word
+};
+
+// Number of 128x256 tiles intersecting the lower triangle of an m x m matrix.
+__host__ __device__ inline int syrk_tile_count(int m) {
+  const int mt = (m + kBM - 1) / kBM;
+  int cnt = 0;
+  for (int i = 0; i < mt; ++i) cnt += (i * kBM + kBM - 1) / kBN + 1;
+  return cnt;
+}
+
+__device__ __forceinline__ void syrk_tile_coords(int t, int& ti, int& tj) {
+  int i = 0;
+  for (;; ++i) {
+    const int c = (i * kBM + kBM - 1) / kBN + 1;
+    if (t < c) break;
+    t -= c;
+  }
+  ti = i;
+  tj = t;
+}
+
+template <int MODE>
+__device__ __forceinline__ void tile_coords(const GemmArgs& g, int t, int& ti, int& tj) {
+  if constexpr (MODE == kBX) {
+    ti = t / g.tiles_n;
+    tj = t - ti * g.tiles_n;
+  } else {
+    syrk_tile_coords(t, ti, tj);
+  }
+}
+
+__device__ __forceinline__ uint4 pack8_bf16(const float* v) {
+  uint4 u;
+  __nv_bfloat162 h0 = __floats2bfloat162_rn(v[0], v[1]);
+  __nv_bfloat162 h1 = __floats2bfloat162_rn(v[2], v[3]);
+  __nv_bfloat162 h2 = __floats2bfloat162_rn(v[4], v[5]);
+  __nv_bfloat162 h3 = __floats2bfloat162_rn(v[6], v[7]);
+  u.x = *reinterpret_cast<uint32_t*>(&h0);
+  u.y = *reinterpret_cast<uint32_t*>(&h1);
+  u.z = *reinterpret_cast<uint32_t*>(&h2);
+  u.w = *reinterpret_cast<uint32_t*>(&h3);
+  return u;
+}
+
+__device__ __forceinline__ void unpack8_bf16(uint4 u, float* v) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&w[i]);
+    float2 f = __bfloat1622float2(h);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+// Load 32 bf16 values of one row starting at column c0 (masked by ncols).
+// `vec` says rows are 16-byte aligned (base and row stride), allowing 16-byte loads.
+__device__ __forceinline__ void load_row32(const __nv_bfloat16* rowp, int c0, int ncols, bool vec,
+                                           float (&v)[32]) {
+  if (vec && c0 + 32 <= ncols) {
+    const uint4* p = reinterpret_cast<const uint4*>(rowp + c0);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) unpack8_bf16(__ldg(p + q), v + 8 * q);
+  } else {
+#pragma unroll
+    for (int k = 0; k < 32; ++k)
+      v[k] = (c0 + k < ncols) ? __bfloat162float(rowp[c0 + k]) : 0.f;
+  }
+}
+
+// Store 32 values of one row (row-major, masked by ncols and an optional
+// lower-triangle predicate col <= row).
+__device__ __forceinline__ void store_row32(__nv_bfloat16* rowp, int c0, int ncols, int row,
+                                            bool lower_only, bool vec, const float (&v)[32]) {
+  const bool full = vec && (c0 + 32 <= ncols) && (!lower_only || c0 + 31 <= row);
+  if (full) {
+    uint4* p = reinterpret_cast<uint4*>(rowp + c0);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) p[q] = pack8_bf16(v + 8 * q);
+  } else {
+#pragma unroll
+    for (int k = 0; k < 32; ++k) {
+      const int c = c0 + k;
+      if (c < ncols && (!lower_only || c <= row)) rowp[c] = __float2bfloat16_rn(v[k]);
+    }
+  }
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(kThreads, 1)
+    ns_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const GemmArgs g) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // 128B-swizzled TMA destinations need 1024-byte alignment.
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* smemA = smem;
+  uint8_t* smemB = smem + kStages * kTileABytes;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+  uint64_t* empty_bar = full_bar + kStages;
+  uint64_t* accf_bar = empty_bar + kStages;  // accumulator ready  [2]
+  uint64_t* acce_bar = accf_bar + 2;         // accumulator drained [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce_bar + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_kb = (g.K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&accf_bar[a], 1);
+      mbar_init(&acce_bar[a], 4);  // one arrive per epilogue warp
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < g.num_tiles && ok; t += gridDim.x) {
+        int ti, tj;
+        tile_coords<MODE>(g, t, ti, tj);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag, g.err, kErrWaitEmpty)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full_bar[stage], kStageBytes);
+          uint8_t* sa = smemA + stage * kTileABytes;
+          uint8_t* sb = smemB + stage * kTileBBytes;
+          tma_load_2d(sa, &tmA, &full_bar[stage], kb * kBK, ti * kBM);
+          if constexpr (MODE == kBX) {
+            // B operand is X (K = rows, N = contiguous columns): four MN-major
+            // boxes of 64 columns x 64 rows, 8 KB apart.
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              tma_load_2d(sb + q * (kBK * 64 * 2), &tmB, &full_bar[stage], tj * kBN + q * 64,
+                          kb * kBK);
+          } else {
+            tma_load_2d(sb, &tmB, &full_bar[stage], kb * kBK, tj * kBN);
+            tma_load_2d(sb + kTileABytes, &tmB, &full_bar[stage], kb * kBK, tj * kBN + kBM);
+          }
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc_bf16(kBM, kBN, 0, MODE == kBX ? 1 : 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < g.num_tiles && ok; t += gridDim.x) {
+        if (!mbar_wait(&acce_bar[acc], acc_phase ^ 1, abort_flag, g.err, kErrWaitAccEmpty)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * kBN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, abort_flag, g.err, kErrWaitFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smemA + stage * kTileABytes);
+          const uint32_t sb = smem_u32(smemB + stage * kTileBBytes);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            // K-major SW128: advance 16 elements = 32 bytes inside the swizzle row.
+            const uint64_t adesc = make_sdesc_sw128(sa + k * 32, 16, 1024);
+            uint64_t bdesc;
+            if constexpr (MODE == kBX) {
+              // MN-major SW128: 16 K-rows = 2048 bytes; LBO = 8 KB between
+              // 64-column chunks, SBO = 1 KB between 8-row groups.
+              bdesc = make_sdesc_sw128(sb + k * 2048, kBK * 64 * 2, 1024);
+            } else {
+              bdesc = make_sdesc_sw128(sb + k * 32, 16, 1024);
+            }
+            tc_mma_bf16(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          tc_commit(&empty_bar[stage]);  // frees the smem stage when these MMAs finish
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        tc_commit(&accf_bar[acc]);  // accumulator complete
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    // 16-byte vector access only when base pointer and row stride allow it
+    const bool out_vec = ((reinterpret_cast<uintptr_t>(g.out) | (g.ld_out * 2)) & 15) == 0;
+    const bool aux_vec = ((reinterpret_cast<uintptr_t>(g.aux) | (g.ld_aux * 2)) & 15) == 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    float dval = 0.f;
+    for (int t = blockIdx.x; t < g.num_tiles; t += gridDim.x) {
+      int ti, tj;
+      tile_coords<MODE>(g, t, ti, tj);
+      if (!mbar_wait(&accf_bar[acc], acc_phase, abort_flag, g.err, kErrWaitAccFull)) break;
+      tc_fence_after();
+      const int row0w = ti * kBM + q * 32;  // first row of this warp
+      const int row = row0w + lane;
+      const bool row_ok = row < g.M;
+      if constexpr (MODE == kBX) dval = row_ok ? g.diag[row] : 0.f;
+#pragma unroll 1
+      for (int c = 0; c < kBN / 32; ++c) {
+        const int c0 = tj * kBN + c * 32;
+        bool need = (c0 < g.N) && (row0w < g.M);
+        if constexpr (MODE != kBX) need = need && (row0w + 31 >= c0);
+        if (!need) continue;  // warp-uniform
+        float v[32];
+        tmem_ld_32x32b_x32(tmem_base + acc * kBN + c * 32 + (static_cast<uint32_t>(q * 32) << 16),
+                           v);
+        if (!row_ok) continue;
+        if constexpr (MODE == kSyrk) {
+          store_row32(g.out + row * g.ld_out, c0, g.N, row, true, out_vec, v);
+          // mirror: (c, row) for c < row; lanes hold consecutive rows -> coalesced
+#pragma unroll
+          for (int k = 0; k < 32; ++k) {
+            const int col = c0 + k;
+            if (col < row && col < g.N)
+              g.out[static_cast<long long>(col) * g.ld_out + row] = __float2bfloat16_rn(v[k]);
+          }
+        } else if constexpr (MODE == kPoly) {
+          float av[32];
+          load_row32(g.aux + row * g.ld_aux, c0, g.N, aux_vec, av);
+#pragma unroll
+          for (int k = 0; k < 32; ++k) {
+            float x = fmaf(kNsC, v[k], kNsB * av[k]);
+            if (c0 + k == row) {
+              g.diag[row] = x + kNsA;
+              x = 0.f;
+            }
+            v[k] = x;
+          }
+          store_row32(g.out + row * g.ld_out, c0, g.N, row, true, out_vec, v);
+#pragma unroll
+          for (int k = 0; k < 32; ++k) {
+            const int col = c0 + k;
+            if (col < row && col < g.N)
+              g.out[static_cast<long long>(col) * g.ld_out + row] = __float2bfloat16_rn(v[k]);
+          }
+        } else {  // kBX
+          float xv[32];
+          load_row32(g.aux + row * g.ld_aux, c0, g.N, aux_vec, xv);
+#pragma unroll
+          for (int k = 0; k < 32; ++k) v[k] = fmaf(dval, xv[k], v[k]);
+          if (g.transpose_out) {
+#pragma unroll
+            for (int k = 0; k < 32; ++k) {
+              const int col = c0 + k;
+              if (col < g.N)
+                g.out[static_cast<long long>(col) * g.ld_out + row] = __float2bfloat16_rn(v[k]);
+            }
+          } else {
+            store_row32(g.out + row * g.ld_out, c0, g.N, row, false, out_vec, v);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acce_bar[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+}  // namespace fm
