@@ -235,9 +235,10 @@ def metric_name(wl: str) -> str:
     return f"FusedMuon.step Newton-Schulz dense-equivalent TFLOP/s, {wl} shape set"
 
 
-def config_for(wl: str, world: int):
+def config_for(wl: str, world: int, shape=SHAPE_NS):
     if wl == "ns":
-        return {"workload": "ns_5step_4096x4096", "shape": list(SHAPE_NS), "ns_steps": NS_STEPS,
+        return {"workload": f"ns_5step_{shape[0]}x{shape[1]}", "shape": list(shape),
+                "ns_steps": NS_STEPS,
                 "seed": 0, "l2": "flushed (256 MB write) before every timed step",
                 "parallelism": "replicas" if world > 1 else "single"}
     shapes = llama_shapes(wl)
@@ -252,7 +253,7 @@ def bench_ns(args, peaks, peak_src):
     from muon_fused import _lib, fused_newton_schulz, workspace_size
 
     dev = torch.device("cuda")
-    m, n = SHAPE_NS
+    m, n = args.shape
     G = torch.randn(m, n, generator=torch.Generator(device=dev).manual_seed(0), device=dev,
                     dtype=torch.bfloat16)
     ws = torch.empty(workspace_size(m, n), dtype=torch.uint8, device=dev)
@@ -302,6 +303,14 @@ def bench_ns(args, peaks, peak_src):
                 "frac": round(achieved / peak, 4), "peak_source": f"{peak_src} bf16_tflops (burst)",
                 "traffic": None, "stages": stages}
 
+    extra = {"us_per_ns": round(ms * 1e3, 1),
+             "useful_tflops": round(NS_STEPS * (m * (m + 1) * n + m * m * (m + 1)
+                                                + 2.0 * m * m * n) / (ms * 1e-3) / 1e12, 1)}
+    if args.quick:
+        return {"ms": ms, "flops": flops, "t_ms": t_ms, "roofline": roofline,
+                "clocks": clk.summary(), "e2e": None, "launches": args.steps * (2 + 3 * NS_STEPS),
+                "extra": extra}
+
     # end to end: pinned host G -> device -> NS -> pinned host result
     G_host = G.cpu().pin_memory()
     out_host = torch.empty((m, n), dtype=torch.bfloat16).pin_memory()
@@ -341,11 +350,8 @@ def bench_ns(args, peaks, peak_src):
                 "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": G_host.nbytes,
                 "d2h_bytes_per_step": out_host.nbytes},
         "launches": args.steps * (2 + 3 * NS_STEPS),
-        "extra": {"us_per_ns": round(ms * 1e3, 1),
-                  "useful_tflops": round(NS_STEPS * (m * (m + 1) * n + m * m * (m + 1)
-                                                     + 2.0 * m * m * n) / (ms * 1e-3) / 1e12, 1),
-                  "torch_eager_gpu_ms": round(eager_ms, 4),
-                  "speedup_vs_torch_eager_gpu": round(eager_ms / ms, 3)},
+        "extra": dict(extra, torch_eager_gpu_ms=round(eager_ms, 4),
+                      speedup_vs_torch_eager_gpu=round(eager_ms / ms, 3)),
     }
 
 
@@ -393,10 +399,14 @@ def bench_muon(args, world, rank, peaks, peak_src):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--workload", choices=["ns", "muon1b", "muon8b"], default=None)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--shape", type=int, nargs=2, default=list(SHAPE_NS),
+                    help="ns workload matrix shape (default: the headline 4096 4096)")
+    ap.add_argument("--quick", action="store_true",
+                    help="ns workload: timed loop and per-kernel pass only (for ncu launch lists)")
     ap.add_argument("--cpu-budget", type=float, default=15.0,
                     help="seconds of host-CPU baseline sampling (rank 0, N=1)")
     args = ap.parse_args()
@@ -416,6 +426,7 @@ def main():
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
     peaks, peak_src = load_peaks()
     if args.workload == "ns":
+        args.shape = tuple(args.shape)
         r = bench_ns(args, peaks, peak_src)
         r["ms"] = barrier_max(r["ms"], world)
         value = world * r["flops"] / (r["ms"] * 1e-3) / 1e12
@@ -430,7 +441,7 @@ def main():
             "ms_per_step": round(r["ms"], 4), "higher_is_better": True,
             "scaling": "weak" if args.workload == "ns" else "strong",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": config_for(args.workload, world),
+            "config": config_for(args.workload, world, getattr(args, "shape", SHAPE_NS)),
             "clocks": r["clocks"], "gpu_launches": r["launches"],
         }
         if r["e2e"] is not None:
@@ -438,7 +449,7 @@ def main():
         if r["roofline"] is not None:
             line["roofline"] = r["roofline"]
         line.update(r["extra"])
-        if world == 1 and args.workload == "ns":
+        if world == 1 and args.workload == "ns" and not args.quick:
             v, sec, calls, threads = cpu_ns_sample(args.cpu_budget)
             line["cpu_baseline"] = {"value": round(v, 4), "unit": "TFLOP/s", "cores": threads,
                                     "kind": "port",
