@@ -94,6 +94,30 @@ int fm_ns_step_debug(const void* X, int64_t m, int64_t n, int64_t ldx, void* A, 
 int fm_device_error(uint32_t* code);
 
 /*
+ * Allocation-free form of fm_fused_newton_schulz, for callers that cannot
+ * call cudaMalloc: code running inside a fixed memory budget (a host
+ * framework that owns all device memory through its own pool), or code on a
+ * path where an allocation could block or fail mid-step.  The caller passes
+ * G and out as for fm_fused_newton_schulz; the scratch is a fixed device
+ * array of FM_STATIC_SCRATCH_BYTES inside the library, which every GPU that
+ * loads the library holds until the process exits.
+ * - Limit: matrices whose fm_workspace_size() exceeds FM_STATIC_SCRATCH_BYTES
+ *   are rejected with FM_E_WORKSPACE (e.g. up to 2048 x 2048 or 1024 x 4096
+ *   fit; 4096 x 4096 does not).
+ * - The first call on each device looks up the array's device address; make
+ *   that first call before capturing the stream into a CUDA graph.
+ * - All calls on a device share the one array, which keeps the last call's
+ *   contents: calls that overlap on the GPU (other streams, other threads)
+ *   race and corrupt each other.  Serialise them on one stream.
+ * - Allocates nothing: no cudaMalloc/cudaFree or allocating library call.
+ * Replaces: nothing; the reference has no counterpart (its binding always
+ * allocates a workspace when none is passed, csrc/torch_binding.cu:93-103).
+ */
+#define FM_STATIC_SCRATCH_BYTES (48ull << 20)
+int fm_fused_newton_schulz_noalloc(const void* G, int dtype, int64_t rows, int64_t cols,
+                                   int64_t ldg, void* out, int steps, void* stream);
+
+/*
  * Benchmark instrumentation.  fm_stage_timing(1) makes every later launch of
  * the calling thread record a CUDA event pair around itself on its stream
  * (fm_stage_timing(0) stops it; either call discards pending pairs).

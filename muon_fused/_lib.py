@@ -31,6 +31,7 @@ SIGNATURES = {
     "fm_newton_schulz_step": (_c_int, [_vp, _i64, _i64, _i64, _vp, _vp, _u64, _vp]),
     "fm_ns_step_debug": (_c_int, [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _u64, _vp]),
     "fm_device_error": (_c_int, [ctypes.POINTER(ctypes.c_uint32)]),
+    "fm_fused_newton_schulz_noalloc": (_c_int, [_vp, _c_int, _i64, _i64, _i64, _vp, _c_int, _vp]),
     "fm_stage_timing": (_c_int, [_c_int]),
     "fm_stage_times": (_c_int, [ctypes.POINTER(ctypes.c_float), ctypes.POINTER(_c_int)]),
 }

@@ -400,6 +400,59 @@ int fm_stage_times(float* ms, int* counts) {
   return FM_OK;
 }
 
+// ---------------------------------------------------------------------------
+// Allocation-free variant of fm_fused_newton_schulz.
+//
+// Its scratch is this file-scope device array instead of a caller buffer.
+// Every GPU that loads the library holds it until the process exits.  Host
+// code cannot use the array's name as a device address, so the address is
+// looked up with cudaGetSymbolAddress once per device, with that device
+// current, on the first call made on that device.
+static __device__ __align__(256) unsigned char g_static_scratch[FM_STATIC_SCRATCH_BYTES];
+
+namespace {
+void* g_static_scratch_ptr[kMaxDevices];
+std::mutex g_static_mu;
+
+int static_scratch(void** out) {
+  int dev = 0;
+  FM_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return fail(FM_E_DEVICE, "device index %d out of range", dev);
+  if (!g_static_scratch_ptr[dev]) {
+    std::lock_guard<std::mutex> lk(g_static_mu);
+    if (!g_static_scratch_ptr[dev]) {
+      void* p = nullptr;
+      FM_CUDA(cudaGetSymbolAddress(&p, g_static_scratch));
+      if (!p) return fail(FM_E_CUDA, "cudaGetSymbolAddress returned a null scratch address");
+      g_static_scratch_ptr[dev] = p;
+    }
+  }
+  *out = g_static_scratch_ptr[dev];
+  return FM_OK;
+}
+}  // namespace
+
+int fm_fused_newton_schulz_noalloc(const void* G, int dtype, int64_t rows, int64_t cols,
+                                   int64_t ldg, void* out, int steps, void* stream) {
+  if (rows > 0 && cols > 0) {
+    uint64_t need = 0;
+    if (int rc = fm_workspace_size(rows, cols, &need)) return rc;
+    if (need > FM_STATIC_SCRATCH_BYTES)
+      return fail(FM_E_WORKSPACE,
+                  "fm_fused_newton_schulz_noalloc: a %lld x %lld matrix needs %llu scratch bytes, "
+                  "more than the library's fixed %llu-byte device scratch; use "
+                  "fm_fused_newton_schulz with a caller-allocated workspace",
+                  (long long)rows, (long long)cols, (unsigned long long)need,
+                  (unsigned long long)FM_STATIC_SCRATCH_BYTES);
+  }
+  void* scratch = nullptr;
+  if (int rc = static_scratch(&scratch)) return rc;
+  // Nothing in the scratch has to start at zero: every byte a call reads
+  // (norm partials, X buffers, A, B, diagonal) is written earlier in the same call.
+  return fm_fused_newton_schulz(G, dtype, rows, cols, ldg, out, steps, scratch,
+                                FM_STATIC_SCRATCH_BYTES, stream);
+}
+
 int fm_device_error(uint32_t* code) {
   if (!code) return fail(FM_E_INVALID, "code is null");
   DeviceState* ds;
