@@ -118,6 +118,16 @@ int fm_fused_newton_schulz_noalloc(const void* G, int dtype, int64_t rows, int64
                                    int64_t ldg, void* out, int steps, void* stream);
 
 /*
+ * GEMM kernel selection for all later calls in the process:
+ * 0 = automatic (CTA-pair 256x256 tiles for matrices with more than 256
+ * rows after orientation, single-CTA 128x256 tiles otherwise),
+ * 1 = always single-CTA, 2 = always CTA pairs.  Both produce the same
+ * arithmetic; the switch exists for tests and tuning.
+ * Replaces: the reference's compile-time tile dispatch, csrc/ns_gemm.cu:68-92.
+ */
+int fm_set_gemm_path(int path);
+
+/*
  * Benchmark instrumentation.  fm_stage_timing(1) makes every later launch of
  * the calling thread record a CUDA event pair around itself on its stream
  * (fm_stage_timing(0) stops it; either call discards pending pairs).

@@ -32,6 +32,7 @@ SIGNATURES = {
     "fm_ns_step_debug": (_c_int, [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _u64, _vp]),
     "fm_device_error": (_c_int, [ctypes.POINTER(ctypes.c_uint32)]),
     "fm_fused_newton_schulz_noalloc": (_c_int, [_vp, _c_int, _i64, _i64, _i64, _vp, _c_int, _vp]),
+    "fm_set_gemm_path": (_c_int, [_c_int]),
     "fm_stage_timing": (_c_int, [_c_int]),
     "fm_stage_times": (_c_int, [ctypes.POINTER(ctypes.c_float), ctypes.POINTER(_c_int)]),
 }
@@ -95,3 +96,8 @@ def stage_times():
     cnt = (ctypes.c_int * 4)()
     check(load().fm_stage_times(ms, cnt), "fm_stage_times")
     return {STAGES[i]: (float(ms[i]), int(cnt[i])) for i in range(4)}
+
+
+def set_gemm_path(path: int) -> None:
+    """0 automatic, 1 single-CTA tiles, 2 CTA-pair tiles (see fm_set_gemm_path)."""
+    check(load().fm_set_gemm_path(int(path)), "fm_set_gemm_path")

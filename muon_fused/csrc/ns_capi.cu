@@ -10,6 +10,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -18,6 +19,7 @@
 #include <vector>
 
 #include "../../include/fused_muon.h"
+#include "ns_gemm2_sm100.cuh"
 #include "ns_gemm_sm100.cuh"
 #include "ns_prep.cuh"
 
@@ -121,6 +123,12 @@ int device_state(DeviceState** out) {
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
       FM_CUDA(cudaFuncSetAttribute(ns_gemm_kernel<kBX>,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
+      FM_CUDA(cudaFuncSetAttribute(ns_gemm_pair_kernel<kSyrk>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, kPairSmemBytes));
+      FM_CUDA(cudaFuncSetAttribute(ns_gemm_pair_kernel<kPoly>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, kPairSmemBytes));
+      FM_CUDA(cudaFuncSetAttribute(ns_gemm_pair_kernel<kBX>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, kPairSmemBytes));
       FM_CUDA(cudaGetSymbolAddress(reinterpret_cast<void**>(&s.err_word), g_device_error));
       if (!g_encode) {
         cudaDriverEntryPointQueryResult q;
@@ -186,6 +194,18 @@ Workspace layout(long long m, long long n, void* base) {
   return w;
 }
 
+// GEMM kernel selection (fm_set_gemm_path): 0 = automatic, 1 = single-CTA
+// 128x256 tiles, 2 = CTA-pair 256x256 tiles.  Automatic uses CTA pairs once
+// the matrix spans more than one 256-row block.
+std::atomic<int> g_gemm_path{0};
+
+bool use_pairs(long long m) {
+  const int p = g_gemm_path.load(std::memory_order_relaxed);
+  if (p == 1) return false;
+  if (p == 2) return true;
+  return m > 256;
+}
+
 template <int MODE>
 int launch_gemm(const DeviceState& ds, const CUtensorMap& ma, const CUtensorMap& mb, GemmArgs g,
                 cudaStream_t st) {
@@ -195,6 +215,32 @@ int launch_gemm(const DeviceState& ds, const CUtensorMap& ma, const CUtensorMap&
   const long long tm = timer_begin(MODE, st);
   ns_gemm_kernel<MODE><<<grid, kThreads, kSmemBytes, st>>>(ma, mb, g);
   FM_CUDA(cudaGetLastError());
+  timer_end(tm, st);
+  return FM_OK;
+}
+
+// CTA-pair launch: a cluster of 2 CTAs per 256x256 tile slot, one pair per
+// two SMs, persistent over the tiles.
+template <int MODE>
+int launch_gemm_pair(const DeviceState& ds, const CUtensorMap& ma, const CUtensorMap& mb,
+                     GemmArgs g, cudaStream_t st) {
+  g.err = ds.err_word;
+  if (g.num_tiles <= 0) return FM_OK;
+  const int pairs = std::min(g.num_tiles, ds.sm_count / 2);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kPairSmemBytes;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const long long tm = timer_begin(MODE, st);
+  FM_CUDA(cudaLaunchKernelEx(&cfg, ns_gemm_pair_kernel<MODE>, ma, mb, g));
   timer_end(tm, st);
   return FM_OK;
 }
@@ -210,32 +256,48 @@ int ns_iteration(const DeviceState& ds, const Workspace& w, const __nv_bfloat16*
   if ((rc = make_map(&mx_mn, cur, m, n, ldc, 64, kBK))) return rc;
   if ((rc = make_map(&ma, w.A, m, m, w.ldm, kBK, kBM))) return rc;
   if ((rc = make_map(&mbm, w.B, m, m, w.ldm, kBK, kBM))) return rc;
+  const bool pairs = use_pairs(m);
 
   // GEMM1: A = X·Xᵀ
   GemmArgs g1{};
   g1.M = int(m); g1.N = int(m); g1.K = int(n);
-  g1.num_tiles = syrk_tile_count(int(m));
   g1.out = w.A; g1.ld_out = w.ldm;
-  if ((rc = launch_gemm<kSyrk>(ds, mx_k, mx_k, g1, st))) return rc;
+  if (pairs) {
+    g1.num_tiles = syrk_pair_tile_count(int(m));
+    rc = launch_gemm_pair<kSyrk>(ds, mx_k, mx_k, g1, st);
+  } else {
+    g1.num_tiles = syrk_tile_count(int(m));
+    rc = launch_gemm<kSyrk>(ds, mx_k, mx_k, g1, st);
+  }
+  if (rc) return rc;
 
   // GEMM2: Boff = offdiag(c·A·A + b·A), diag = a + diag(c·A·A + b·A)
   GemmArgs g2{};
   g2.M = int(m); g2.N = int(m); g2.K = int(m);
-  g2.num_tiles = syrk_tile_count(int(m));
   g2.out = w.B; g2.ld_out = w.ldm;
   g2.aux = w.A; g2.ld_aux = w.ldm;
   g2.diag = w.diag;
-  if ((rc = launch_gemm<kPoly>(ds, ma, ma, g2, st))) return rc;
+  if (pairs) {
+    g2.num_tiles = syrk_pair_tile_count(int(m));
+    rc = launch_gemm_pair<kPoly>(ds, ma, ma, g2, st);
+  } else {
+    g2.num_tiles = syrk_tile_count(int(m));
+    rc = launch_gemm<kPoly>(ds, ma, ma, g2, st);
+  }
+  if (rc) return rc;
 
   // GEMM3: X' = diag ⊙ X + Boff·X
   GemmArgs g3{};
   g3.M = int(m); g3.N = int(n); g3.K = int(m);
-  g3.tiles_n = int((n + kBN - 1) / kBN);
-  g3.num_tiles = int((m + kBM - 1) / kBM) * g3.tiles_n;
   g3.out = nxt; g3.ld_out = out_ld; g3.transpose_out = transpose_out;
   g3.aux = cur; g3.ld_aux = ldc;
   g3.diag = w.diag;
-  return launch_gemm<kBX>(ds, mbm, mx_mn, g3, st);
+  const int bm = pairs ? kPairBM : kBM, bn = pairs ? kPairBN : kBN;
+  g3.tiles_n = int((n + bn - 1) / bn);
+  g3.tiles_m = int((m + bm - 1) / bm);
+  g3.num_tiles = g3.tiles_m * g3.tiles_n;
+  return pairs ? launch_gemm_pair<kBX>(ds, mbm, mx_mn, g3, st)
+               : launch_gemm<kBX>(ds, mbm, mx_mn, g3, st);
 }
 
 int check_dims(long long rows, long long cols) {
@@ -370,6 +432,12 @@ int fm_ns_step_debug(const void* X, int64_t m, int64_t n, int64_t ldx, void* A, 
   FM_CUDA(cudaMemcpy2DAsync(A, m * 2, w.A, w.ldm * 2, m * 2, m, cudaMemcpyDeviceToDevice, st));
   FM_CUDA(cudaMemcpy2DAsync(Boff, m * 2, w.B, w.ldm * 2, m * 2, m, cudaMemcpyDeviceToDevice, st));
   FM_CUDA(cudaMemcpyAsync(diag, w.diag, m * 4, cudaMemcpyDeviceToDevice, st));
+  return FM_OK;
+}
+
+int fm_set_gemm_path(int path) {
+  if (path < 0 || path > 2) return fail(FM_E_INVALID, "gemm path must be 0, 1 or 2, got %d", path);
+  g_gemm_path.store(path);
   return FM_OK;
 }
 

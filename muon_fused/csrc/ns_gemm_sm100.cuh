@@ -57,6 +57,7 @@ struct GemmArgs {
   int K;          // reduction length: n for kSyrk, m otherwise
   int num_tiles;  // scheduled tiles
   int tiles_n;    // kBX: column tiles per row block
+  int tiles_m;    // kBX: row tiles per column block
   __nv_bfloat16* out;
   long long ld_out;
   const __nv_bfloat16* aux;  // kPoly: A (for b·A); kBX: X (for d ⊙ X)
@@ -88,8 +89,11 @@ __device__ __forceinline__ void syrk_tile_coords(int t, int& ti, int& tj) {
 template <int MODE>
 __device__ __forceinline__ void tile_coords(const GemmArgs& g, int t, int& ti, int& tj) {
   if constexpr (MODE == kBX) {
-    ti = t / g.tiles_n;
-    tj = t - ti * g.tiles_n;
+    // Column-block-major: concurrent CTAs share a few column blocks of X (the
+    // larger operand, streamed once) and sweep all row blocks of B (m x m,
+    // the smaller one, which stays in L2).
+    tj = t / g.tiles_m;
+    ti = t - tj * g.tiles_m;
   } else {
     syrk_tile_coords(t, ti, tj);
   }
@@ -134,6 +138,41 @@ __device__ __forceinline__ void load_row32(const __nv_bfloat16* rowp, int c0, in
   }
 }
 
+// Raw (still packed bf16) form of load_row32, so a chunk can be fetched one
+// step ahead of its use without spending 32 registers on it.
+__device__ __forceinline__ void load_raw32(const __nv_bfloat16* rowp, int c0, int ncols, bool vec,
+                                           uint4 (&r)[4]) {
+  if (vec && c0 + 32 <= ncols) {
+    const uint4* p = reinterpret_cast<const uint4*>(rowp + c0);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) r[q] = __ldg(p + q);
+  } else {
+    uint16_t h[32];
+#pragma unroll
+    for (int k = 0; k < 32; ++k)
+      h[k] = (c0 + k < ncols) ? __bfloat16_as_ushort(rowp[c0 + k]) : static_cast<uint16_t>(0);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      r[q].x = h[8 * q + 0] | (static_cast<uint32_t>(h[8 * q + 1]) << 16);
+      r[q].y = h[8 * q + 2] | (static_cast<uint32_t>(h[8 * q + 3]) << 16);
+      r[q].z = h[8 * q + 4] | (static_cast<uint32_t>(h[8 * q + 5]) << 16);
+      r[q].w = h[8 * q + 6] | (static_cast<uint32_t>(h[8 * q + 7]) << 16);
+    }
+  }
+}
+
+// Mirror of a lower-triangle chunk: value (row, c) also goes to (c, row) for
+// c < row.  Lanes hold consecutive rows, so each store instruction writes 64
+// contiguous bytes of row c.
+__device__ __forceinline__ void store_mirror32(__nv_bfloat16* out, long long ld, int c0, int ncols,
+                                               int row, const float (&v)[32]) {
+#pragma unroll
+  for (int k = 0; k < 32; ++k) {
+    const int col = c0 + k;
+    if (col < row && col < ncols) out[static_cast<long long>(col) * ld + row] = __float2bfloat16_rn(v[k]);
+  }
+}
+
 // Store 32 values of one row (row-major, masked by ncols and an optional
 // lower-triangle predicate col <= row).
 __device__ __forceinline__ void store_row32(__nv_bfloat16* rowp, int c0, int ncols, int row,
@@ -150,6 +189,90 @@ __device__ __forceinline__ void store_row32(__nv_bfloat16* rowp, int c0, int nco
       if (c < ncols && (!lower_only || c <= row)) rowp[c] = __float2bfloat16_rn(v[k]);
     }
   }
+}
+
+// Epilogue of one accumulator tile for one warp: TMEM lane quarter q holds
+// rows row0w .. row0w+31 of the output; the tile's columns start at col0 and
+// the accumulator's first TMEM column is tmem_acc.  Waits for the
+// accumulator on accf_bar (parity acc_phase), returns false if that wait
+// gave up.  Shared by the 1-CTA and the 2-CTA kernels.
+template <int MODE>
+__device__ __forceinline__ bool epilogue_tile(const GemmArgs& g, uint32_t tmem_acc, int q,
+                                              int row0w, int col0, int lane, bool out_vec,
+                                              bool aux_vec, uint64_t* accf_bar, uint32_t acc_phase,
+                                              volatile int* abort_flag) {
+  const int row = row0w + lane;
+  const bool row_ok = row < g.M;
+  const __nv_bfloat16* aux_row = g.aux + static_cast<long long>(row) * g.ld_aux;
+  // Chunks of 32 columns this warp stores: a prefix 0..nc-1 (columns below N;
+  // for the SYRK modes also at or left of the warp's last row).
+  int col_end = min(g.N, col0 + kBN);
+  if constexpr (MODE != kBX) col_end = min(col_end, row0w + 32);
+  const int nc = row0w < g.M ? max(0, (col_end - col0 + 31) / 32) : 0;
+  // The epilogue operand (A for kPoly, X for kBX) does not depend on the
+  // accumulator: fetch the first chunk before waiting for the MMAs and each
+  // next chunk while the current one is processed.
+  uint4 araw[4], anext[4];
+  if constexpr (MODE != kSyrk) {
+    if (nc > 0 && row_ok) load_raw32(aux_row, col0, g.N, aux_vec, araw);
+  }
+  float dval = 0.f;
+  if constexpr (MODE == kBX) dval = row_ok ? g.diag[row] : 0.f;
+  if (!mbar_wait(accf_bar, acc_phase, abort_flag, g.err, kErrWaitAccFull)) return false;
+  tc_fence_after();
+#pragma unroll 1
+  for (int c = 0; c < nc; ++c) {
+    const int c0 = col0 + c * 32;
+    if constexpr (MODE != kSyrk) {
+      if (c + 1 < nc && row_ok) load_raw32(aux_row, c0 + 32, g.N, aux_vec, anext);
+    }
+    float v[32];
+    tmem_ld_32x32b_x32(tmem_acc + c * 32 + (static_cast<uint32_t>(q * 32) << 16), v);
+    if (row_ok) {
+      if constexpr (MODE == kSyrk) {
+        store_row32(g.out + row * g.ld_out, c0, g.N, row, true, out_vec, v);
+        store_mirror32(g.out, g.ld_out, c0, g.N, row, v);
+      } else if constexpr (MODE == kPoly) {
+        float av[32];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) unpack8_bf16(araw[k], av + 8 * k);
+#pragma unroll
+        for (int k = 0; k < 32; ++k) {
+          float x = fmaf(kNsC, v[k], kNsB * av[k]);
+          if (c0 + k == row) {
+            g.diag[row] = x + kNsA;
+            x = 0.f;
+          }
+          v[k] = x;
+        }
+        store_row32(g.out + row * g.ld_out, c0, g.N, row, true, out_vec, v);
+        store_mirror32(g.out, g.ld_out, c0, g.N, row, v);
+      } else {  // kBX
+        float xv[32];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) unpack8_bf16(araw[k], xv + 8 * k);
+#pragma unroll
+        for (int k = 0; k < 32; ++k) v[k] = fmaf(dval, xv[k], v[k]);
+        if (g.transpose_out) {
+#pragma unroll
+          for (int k = 0; k < 32; ++k) {
+            const int col = c0 + k;
+            if (col < g.N)
+              g.out[static_cast<long long>(col) * g.ld_out + row] = __float2bfloat16_rn(v[k]);
+          }
+        } else {
+          store_row32(g.out + row * g.ld_out, c0, g.N, row, false, out_vec, v);
+        }
+      }
+    }
+    if constexpr (MODE != kSyrk) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) araw[k] = anext[k];
+    }
+  }
+  tc_fence_before();
+  __syncwarp();
+  return true;
 }
 
 template <int MODE>
@@ -292,73 +415,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool aux_vec = ((reinterpret_cast<uintptr_t>(g.aux) | (g.ld_aux * 2)) & 15) == 0;
     int acc = 0;
     uint32_t acc_phase = 0;
-    float dval = 0.f;
     for (int t = blockIdx.x; t < g.num_tiles; t += gridDim.x) {
       int ti, tj;
       tile_coords<MODE>(g, t, ti, tj);
-      if (!mbar_wait(&accf_bar[acc], acc_phase, abort_flag, g.err, kErrWaitAccFull)) break;
-      tc_fence_after();
-      const int row0w = ti * kBM + q * 32;  // first row of this warp
-      const int row = row0w + lane;
-      const bool row_ok = row < g.M;
-      if constexpr (MODE == kBX) dval = row_ok ? g.diag[row] : 0.f;
-#pragma unroll 1
-      for (int c = 0; c < kBN / 32; ++c) {
-        const int c0 = tj * kBN + c * 32;
-        bool need = (c0 < g.N) && (row0w < g.M);
-        if constexpr (MODE != kBX) need = need && (row0w + 31 >= c0);
-        if (!need) continue;  // warp-uniform
-        float v[32];
-        tmem_ld_32x32b_x32(tmem_base + acc * kBN + c * 32 + (static_cast<uint32_t>(q * 32) << 16),
-                           v);
-        if (!row_ok) continue;
-        if constexpr (MODE == kSyrk) {
-          store_row32(g.out + row * g.ld_out, c0, g.N, row, true, out_vec, v);
-          // mirror: (c, row) for c < row; lanes hold consecutive rows -> coalesced
-#pragma unroll
-          for (int k = 0; k < 32; ++k) {
-            const int col = c0 + k;
-            if (col < row && col < g.N)
-              g.out[static_cast<long long>(col) * g.ld_out + row] = __float2bfloat16_rn(v[k]);
-          }
-        } else if constexpr (MODE == kPoly) {
-          float av[32];
-          load_row32(g.aux + row * g.ld_aux, c0, g.N, aux_vec, av);
-#pragma unroll
-          for (int k = 0; k < 32; ++k) {
-            float x = fmaf(kNsC, v[k], kNsB * av[k]);
-            if (c0 + k == row) {
-              g.diag[row] = x + kNsA;
-              x = 0.f;
-            }
-            v[k] = x;
-          }
-          store_row32(g.out + row * g.ld_out, c0, g.N, row, true, out_vec, v);
-#pragma unroll
-          for (int k = 0; k < 32; ++k) {
-            const int col = c0 + k;
-            if (col < row && col < g.N)
-              g.out[static_cast<long long>(col) * g.ld_out + row] = __float2bfloat16_rn(v[k]);
-          }
-        } else {  // kBX
-          float xv[32];
-          load_row32(g.aux + row * g.ld_aux, c0, g.N, aux_vec, xv);
-#pragma unroll
-          for (int k = 0; k < 32; ++k) v[k] = fmaf(dval, xv[k], v[k]);
-          if (g.transpose_out) {
-#pragma unroll
-            for (int k = 0; k < 32; ++k) {
-              const int col = c0 + k;
-              if (col < g.N)
-                g.out[static_cast<long long>(col) * g.ld_out + row] = __float2bfloat16_rn(v[k]);
-            }
-          } else {
-            store_row32(g.out + row * g.ld_out, c0, g.N, row, false, out_vec, v);
-          }
-        }
-      }
-      tc_fence_before();
-      __syncwarp();
+      if (!epilogue_tile<MODE>(g, tmem_base + acc * kBN, q, ti * kBM + q * 32, tj * kBN, lane,
+                               out_vec, aux_vec, &accf_bar[acc], acc_phase, abort_flag))
+        break;
       if (lane == 0) mbar_arrive(&acce_bar[acc]);
       if (++acc == 2) {
         acc = 0;
