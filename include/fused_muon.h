@@ -63,6 +63,21 @@ int fm_fused_newton_schulz(const void* G, int dtype, int64_t rows, int64_t cols,
                            void* stream);
 
 /*
+ * Batched form: `batch` same-shape matrices G_b = G + b * batch_stride_g
+ * (elements), each orthogonalised independently into
+ * out + b * batch_stride_out (bf16, rows x cols contiguous per matrix).  One
+ * set of GEMM launches covers the whole batch, so small matrices fill the GPU.
+ * workspace: at least fm_workspace_size_batched(batch, rows, cols) bytes.
+ * Replaces: the reference's per-matrix loop of fused_newton_schulz calls
+ * inside FusedMuon.step (muon_fused/optimizer.py:128-163).
+ */
+int fm_workspace_size_batched(int64_t batch, int64_t rows, int64_t cols, uint64_t* bytes);
+int fm_fused_newton_schulz_batched(const void* G, int dtype, int64_t batch, int64_t rows,
+                                   int64_t cols, int64_t ldg, int64_t batch_stride_g, void* out,
+                                   int64_t batch_stride_out, int steps, void* workspace,
+                                   uint64_t workspace_bytes, void* stream);
+
+/*
  * One Newton-Schulz iteration on an already normalised bf16 matrix:
  * X_new = (a·I + b·A + c·A²)·X with A = X·Xᵀ.  X: m x n bf16 with row stride
  * ldx; X_new: m x n bf16, contiguous.  No transpose is applied.
@@ -102,7 +117,7 @@ int fm_device_error(uint32_t* code);
  * array of FM_STATIC_SCRATCH_BYTES inside the library, which every GPU that
  * loads the library holds until the process exits.
  * - Limit: matrices whose fm_workspace_size() exceeds FM_STATIC_SCRATCH_BYTES
- *   are rejected with FM_E_WORKSPACE (e.g. up to 2048 x 2048 or 1024 x 4096
+ *   are rejected with FM_E_WORKSPACE (e.g. 2048 x 2048 or 1024 x 4096
  *   fit; 4096 x 4096 does not).
  * - The first call on each device looks up the array's device address; make
  *   that first call before capturing the stream into a CUDA graph.
@@ -113,9 +128,34 @@ int fm_device_error(uint32_t* code);
  * Replaces: nothing; the reference has no counterpart (its binding always
  * allocates a workspace when none is passed, csrc/torch_binding.cu:93-103).
  */
-#define FM_STATIC_SCRATCH_BYTES (48ull << 20)
+#define FM_STATIC_SCRATCH_BYTES (64ull << 20)
 int fm_fused_newton_schulz_noalloc(const void* G, int dtype, int64_t rows, int64_t cols,
                                    int64_t ldg, void* out, int steps, void* stream);
+
+/*
+ * Muon momentum in one pass over n elements of dtype FM_DT_F32 / BF16 / F16:
+ *   buf = round(round(buf * momentum) + grad)
+ *   dir = bf16(round(grad + momentum * buf))   if nesterov
+ *   dir = bf16(buf)                            otherwise
+ * where round() is rounding to the buffer's dtype after each torch op of the
+ * reference, so buf is bit-identical to the reference's; dir is the bf16
+ * Newton-Schulz input (the reference casts to bf16 inside NS, ns_step.py:40).
+ * Replaces: muon_fused/optimizer.py:139-149 (buf.mul_(mu).add_(g);
+ * g.add(buf, alpha=mu)).
+ */
+int fm_muon_momentum(void* buf, const void* grad, void* dir, int64_t n, int dtype, float momentum,
+                     int nesterov, void* stream);
+
+/*
+ * Decoupled weight decay + update in one pass: for n elements of the
+ * parameter (dtype FM_DT_F32 / BF16 / F16) and the bf16 update u,
+ *   p = round(round(p * decay) + alpha * u)
+ * with decay = 1 - lr*wd and alpha = -lr * 0.2 * sqrt(max(A, B)).
+ * Replaces: muon_fused/optimizer.py:157-163 (p.data.mul_(1 - lr*wd);
+ * p.data.add_(u, alpha=-adjusted_lr)).
+ */
+int fm_muon_apply(void* param, int dtype, const void* update, int64_t n, float decay, float alpha,
+                  void* stream);
 
 /*
  * GEMM kernel selection for all later calls in the process:

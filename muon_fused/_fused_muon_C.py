@@ -75,6 +75,44 @@ def fused_newton_schulz(G: torch.Tensor, steps: int = 5, workspace=None) -> torc
     return out
 
 
+def workspace_size_batched(batch: int, m: int, n: int) -> int:
+    """Workspace bytes for ``batch`` same-shape (m, n) matrices."""
+    return _lib.workspace_bytes_batched(batch, m, n)
+
+
+def fused_newton_schulz_batched(G: torch.Tensor, steps: int = 5, workspace=None,
+                                out: torch.Tensor | None = None) -> torch.Tensor:
+    """Newton-Schulz on each matrix of a (batch, rows, cols) tensor in one set of
+    GEMM launches; returns a bf16 (batch, rows, cols) tensor (or writes ``out``,
+    which must be a contiguous bf16 tensor of that shape)."""
+    _check_cuda(G, "G")
+    if G.dim() != 3:
+        raise RuntimeError("G must be 3D (batch, rows, cols)")
+    if G.dtype not in _DTYPE_CODE:
+        raise RuntimeError(f"unsupported dtype {G.dtype}; expected a floating type")
+    if G.stride(2) != 1 or G.stride(0) < G.shape[1] * G.stride(1):
+        G = G.contiguous()
+    batch, rows, cols = G.shape
+    if out is None:
+        out = torch.empty((batch, rows, cols), dtype=torch.bfloat16, device=G.device)
+    elif (out.shape != G.shape or out.dtype != torch.bfloat16 or not out.is_contiguous()
+          or out.device != G.device):
+        raise RuntimeError("out must be a contiguous bf16 tensor shaped like G on its device")
+    if G.numel() == 0:
+        return out
+    need = _lib.workspace_bytes_batched(batch, rows, cols)
+    if workspace is None or workspace.nbytes < need:
+        workspace = torch.empty(need, dtype=torch.uint8, device=G.device)
+    with torch.cuda.device(G.device):
+        _lib.check(
+            _lib.load().fm_fused_newton_schulz_batched(
+                G.data_ptr(), _DTYPE_CODE[G.dtype], batch, rows, cols, G.stride(1), G.stride(0),
+                out.data_ptr(), rows * cols, int(steps), workspace.data_ptr(), workspace.nbytes,
+                _stream(G)),
+            "fm_fused_newton_schulz_batched")
+    return out
+
+
 def newton_schulz_step(X: torch.Tensor, workspace=None) -> torch.Tensor:
     """One iteration on a normalised bf16 matrix: (aI + bA + cA²)·X, A = X·Xᵀ.
 

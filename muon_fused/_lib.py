@@ -28,10 +28,15 @@ SIGNATURES = {
     "fm_last_error": (ctypes.c_char_p, []),
     "fm_workspace_size": (_c_int, [_i64, _i64, ctypes.POINTER(_u64)]),
     "fm_fused_newton_schulz": (_c_int, [_vp, _c_int, _i64, _i64, _i64, _vp, _c_int, _vp, _u64, _vp]),
+    "fm_workspace_size_batched": (_c_int, [_i64, _i64, _i64, ctypes.POINTER(_u64)]),
+    "fm_fused_newton_schulz_batched": (_c_int, [_vp, _c_int, _i64, _i64, _i64, _i64, _i64, _vp,
+                                                _i64, _c_int, _vp, _u64, _vp]),
     "fm_newton_schulz_step": (_c_int, [_vp, _i64, _i64, _i64, _vp, _vp, _u64, _vp]),
     "fm_ns_step_debug": (_c_int, [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _u64, _vp]),
     "fm_device_error": (_c_int, [ctypes.POINTER(ctypes.c_uint32)]),
     "fm_fused_newton_schulz_noalloc": (_c_int, [_vp, _c_int, _i64, _i64, _i64, _vp, _c_int, _vp]),
+    "fm_muon_momentum": (_c_int, [_vp, _vp, _vp, _i64, _c_int, ctypes.c_float, _c_int, _vp]),
+    "fm_muon_apply": (_c_int, [_vp, _c_int, _vp, _i64, ctypes.c_float, ctypes.c_float, _vp]),
     "fm_set_gemm_path": (_c_int, [_c_int]),
     "fm_stage_timing": (_c_int, [_c_int]),
     "fm_stage_times": (_c_int, [ctypes.POINTER(ctypes.c_float), ctypes.POINTER(_c_int)]),
@@ -74,6 +79,13 @@ def check(rc: int, what: str) -> None:
 def workspace_bytes(rows: int, cols: int) -> int:
     out = ctypes.c_uint64(0)
     check(load().fm_workspace_size(int(rows), int(cols), ctypes.byref(out)), "fm_workspace_size")
+    return int(out.value)
+
+
+def workspace_bytes_batched(batch: int, rows: int, cols: int) -> int:
+    out = ctypes.c_uint64(0)
+    check(load().fm_workspace_size_batched(int(batch), int(rows), int(cols), ctypes.byref(out)),
+          "fm_workspace_size_batched")
     return int(out.value)
 
 

@@ -21,6 +21,7 @@
 #include "../../include/fused_muon.h"
 #include "ns_gemm2_sm100.cuh"
 #include "ns_gemm_sm100.cuh"
+#include "muon_elementwise.cuh"
 #include "ns_prep.cuh"
 
 namespace fm {
@@ -145,18 +146,21 @@ int device_state(DeviceState** out) {
   return FM_OK;
 }
 
-// 2-D bf16 tensor map over a rows x cols row-major matrix with row stride ld
-// (elements), box = box_cols (inner) x box_rows, 128-byte swizzle, zero fill
-// out of bounds.
-int make_map(CUtensorMap* map, const void* base, long long rows, long long cols, long long ld,
-             int box_cols, int box_rows) {
-  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (ld * 2) % 16 != 0)
-    return fail(FM_E_INVALID, "TMA operand must be 16-byte aligned with 16-byte row stride");
-  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * 2)};
-  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
+// 3-D bf16 tensor map over `batch` row-major rows x cols matrices with row
+// stride ld and matrix stride bstride (elements); box = box_cols (inner) x
+// box_rows x 1, 128-byte swizzle, zero fill out of bounds.
+int make_map(CUtensorMap* map, const void* base, long long batch, long long rows, long long cols,
+             long long ld, long long bstride, int box_cols, int box_rows) {
+  if (batch == 1) bstride = round_up(rows * ld, 8);
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (ld * 2) % 16 != 0 ||
+      (bstride * 2) % 16 != 0)
+    return fail(FM_E_INVALID, "TMA operand must be 16-byte aligned with 16-byte row/matrix strides");
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows),
+                        static_cast<cuuint64_t>(batch)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld * 2), static_cast<cuuint64_t>(bstride * 2)};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows), 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims,
                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -164,24 +168,94 @@ int make_map(CUtensorMap* map, const void* base, long long rows, long long cols,
   return FM_OK;
 }
 
-// Workspace carve-up for an m x n problem (m <= n after orientation).
+// GEMM kernel selection (fm_set_gemm_path): 0 = automatic, 1 = single-CTA
+// 128x256 tiles, 2 = CTA-pair 256x256 tiles.  Automatic uses CTA pairs for
+// batches and once the matrix spans more than one 256-row block.
+std::atomic<int> g_gemm_path{0};
+
+// CTA pairs of a 148-SM B200.  Split-K choices (and therefore workspace
+// sizes) are made against this constant so fm_workspace_size needs no device.
+constexpr int kRefPairs = 74;
+
+struct GemmPlan {
+  int tiles = 0;  // output tiles per matrix
+  int split = 1;  // K-splits per tile
+  int kbps = 0;   // K-blocks per split
+};
+
+struct NsPlan {
+  bool pairs = false;
+  GemmPlan g[3];  // X·Xᵀ, polynomial, B·X
+  int tiles_m3 = 0, tiles_n3 = 0;
+  long long split_slots = 0;  // max over GEMMs of batch*tiles*split (split > 1 only)
+  long long counter_slots = 0;
+};
+
+// Split-K when a launch has fewer tiles than CTA pairs: at most 8 splits, at
+// least 4 K-blocks (256 reduction elements) per split, no empty split.
+GemmPlan plan_gemm(long long tiles, long long batch, int num_kb, bool pairs) {
+  GemmPlan p;
+  p.tiles = int(tiles);
+  p.kbps = num_kb;
+  const long long units = tiles * batch;
+  if (!pairs || units >= kRefPairs) return p;
+  int s = int(std::min<long long>(8, kRefPairs / units));
+  s = std::min(s, std::max(1, num_kb / 4));
+  if (s <= 1) return p;
+  const int kbps = (num_kb + s - 1) / s;
+  p.split = (num_kb + kbps - 1) / kbps;
+  p.kbps = kbps;
+  return p;
+}
+
+NsPlan plan_ns(long long batch, long long m, long long n, int path) {
+  NsPlan P;
+  P.pairs = path == 2 || (path == 0 && (m > 256 || batch > 1));
+  const int kb1 = int((n + kBK - 1) / kBK), kb2 = int((m + kBK - 1) / kBK);
+  const int bm = P.pairs ? kPairBM : kBM, bn = P.pairs ? kPairBN : kBN;
+  const int t1 = P.pairs ? syrk_pair_tile_count(int(m)) : syrk_tile_count(int(m));
+  P.tiles_m3 = int((m + bm - 1) / bm);
+  P.tiles_n3 = int((n + bn - 1) / bn);
+  P.g[0] = plan_gemm(t1, batch, kb1, P.pairs);
+  P.g[1] = plan_gemm(t1, batch, kb2, P.pairs);
+  P.g[2] = plan_gemm(static_cast<long long>(P.tiles_m3) * P.tiles_n3, batch, kb2, P.pairs);
+  for (const GemmPlan& g : P.g) {
+    if (g.split > 1) {
+      P.split_slots = std::max(P.split_slots, batch * g.tiles * g.split);
+      P.counter_slots = std::max(P.counter_slots, batch * g.tiles);
+    }
+  }
+  return P;
+}
+
+// Workspace carve-up for `batch` m x n problems (m <= n after orientation).
 struct Workspace {
   __nv_bfloat16* X[2];
   __nv_bfloat16* A;
   __nv_bfloat16* B;
   float* diag;
-  float* partials;
-  long long ldx, ldm;
+  float* partials;  // Frobenius-norm partials, kMaxPartials per matrix
+  float* splitk;    // split-K fp32 partial tiles (128 KB per unit and CTA)
+  int* counters;    // split-K arrival counters (two per tile: one per CTA)
+  long long ldx, ldm, xs, ms, dsz;  // row strides and per-matrix strides (elements)
+  size_t counter_bytes;
   size_t bytes;
 };
 
-Workspace layout(long long m, long long n, void* base) {
+Workspace layout(long long batch, long long m, long long n, void* base) {
   Workspace w{};
   w.ldx = round_up(n, 8);
   w.ldm = round_up(m, 8);
+  w.xs = round_up(m * w.ldx, 128);
+  w.ms = round_up(m * w.ldm, 128);
+  w.dsz = round_up(m, 64);
+  // sized for the CTA-pair path, the larger of the two
+  const NsPlan P = plan_ns(batch, m, n, 2);
   auto a256 = [](size_t b) { return (b + 255) & ~size_t(255); };
-  const size_t xb = a256(size_t(m) * w.ldx * 2), mb = a256(size_t(m) * w.ldm * 2);
-  const size_t db = a256(size_t(m) * 4), pb = a256(kMaxPartials * 4);
+  const size_t xb = a256(size_t(batch) * w.xs * 2), mb = a256(size_t(batch) * w.ms * 2);
+  const size_t db = a256(size_t(batch) * w.dsz * 4), pb = a256(size_t(batch) * kMaxPartials * 4);
+  const size_t sb = a256(size_t(P.split_slots) * 2 * kPartialFloats * 4);
+  w.counter_bytes = a256(size_t(P.counter_slots) * 2 * 4);
   char* p = static_cast<char*>(base);
   size_t off = 0;
   w.X[0] = reinterpret_cast<__nv_bfloat16*>(p + off); off += xb;
@@ -190,20 +264,10 @@ Workspace layout(long long m, long long n, void* base) {
   w.B = reinterpret_cast<__nv_bfloat16*>(p + off); off += mb;
   w.diag = reinterpret_cast<float*>(p + off); off += db;
   w.partials = reinterpret_cast<float*>(p + off); off += pb;
+  w.splitk = reinterpret_cast<float*>(p + off); off += sb;
+  w.counters = reinterpret_cast<int*>(p + off); off += w.counter_bytes;
   w.bytes = off;
   return w;
-}
-
-// GEMM kernel selection (fm_set_gemm_path): 0 = automatic, 1 = single-CTA
-// 128x256 tiles, 2 = CTA-pair 256x256 tiles.  Automatic uses CTA pairs once
-// the matrix spans more than one 256-row block.
-std::atomic<int> g_gemm_path{0};
-
-bool use_pairs(long long m) {
-  const int p = g_gemm_path.load(std::memory_order_relaxed);
-  if (p == 1) return false;
-  if (p == 2) return true;
-  return m > 256;
 }
 
 template <int MODE>
@@ -220,7 +284,7 @@ int launch_gemm(const DeviceState& ds, const CUtensorMap& ma, const CUtensorMap&
 }
 
 // CTA-pair launch: a cluster of 2 CTAs per 256x256 tile slot, one pair per
-// two SMs, persistent over the tiles.
+// two SMs, persistent over the work units.
 template <int MODE>
 int launch_gemm_pair(const DeviceState& ds, const CUtensorMap& ma, const CUtensorMap& mb,
                      GemmArgs g, cudaStream_t st) {
@@ -245,59 +309,80 @@ int launch_gemm_pair(const DeviceState& ds, const CUtensorMap& ma, const CUtenso
   return FM_OK;
 }
 
-// One iteration: cur (m x n, ld w.ldx or given) -> nxt.
-// out_ld / transpose_out describe how X' is stored.
-int ns_iteration(const DeviceState& ds, const Workspace& w, const __nv_bfloat16* cur, long long ldc,
-                 long long m, long long n, __nv_bfloat16* nxt, long long out_ld, int transpose_out,
-                 cudaStream_t st) {
+// Operands of one iteration for a batch: X (cur) -> X' (nxt).
+struct IterIO {
+  const __nv_bfloat16* cur;
+  long long ldc, cur_bs;  // row / matrix stride of cur
+  __nv_bfloat16* nxt;
+  long long out_ld, out_bs;  // row / matrix stride of nxt (of X'ᵀ when transposed)
+  int transpose_out;
+};
+
+template <int MODE>
+int run_gemm(const DeviceState& ds, const NsPlan& P, const GemmPlan& gp, long long batch,
+             const CUtensorMap& ma, const CUtensorMap& mb, GemmArgs g, cudaStream_t st) {
+  g.batch = int(batch);
+  g.tiles = gp.tiles;
+  g.split = gp.split;
+  g.kb_per_split = gp.kbps;
+  g.num_tiles = int(batch * gp.tiles * gp.split);
+  if (P.pairs) return launch_gemm_pair<MODE>(ds, ma, mb, g, st);
+  g.num_tiles = gp.tiles;  // single-CTA kernel: batch == 1, split == 1
+  return launch_gemm<MODE>(ds, ma, mb, g, st);
+}
+
+int ns_iteration(const DeviceState& ds, const Workspace& w, const NsPlan& P, long long batch,
+                 long long m, long long n, const IterIO& io, cudaStream_t st) {
+  if (!P.pairs && batch > 1) {
+    // single-CTA path (tests / tuning only): one matrix at a time
+    for (long long b = 0; b < batch; ++b) {
+      Workspace wb = w;
+      wb.A = w.A + b * w.ms;
+      wb.B = w.B + b * w.ms;
+      wb.diag = w.diag + b * w.dsz;
+      IterIO ib = io;
+      ib.cur = io.cur + b * io.cur_bs;
+      ib.nxt = io.nxt + b * io.out_bs;
+      if (int rc = ns_iteration(ds, wb, P, 1, m, n, ib, st)) return rc;
+    }
+    return FM_OK;
+  }
   CUtensorMap mx_k, mx_mn, ma, mbm;
   int rc;
-  if ((rc = make_map(&mx_k, cur, m, n, ldc, kBK, kBM))) return rc;
-  if ((rc = make_map(&mx_mn, cur, m, n, ldc, 64, kBK))) return rc;
-  if ((rc = make_map(&ma, w.A, m, m, w.ldm, kBK, kBM))) return rc;
-  if ((rc = make_map(&mbm, w.B, m, m, w.ldm, kBK, kBM))) return rc;
-  const bool pairs = use_pairs(m);
+  if ((rc = make_map(&mx_k, io.cur, batch, m, n, io.ldc, io.cur_bs, kBK, kBM))) return rc;
+  if ((rc = make_map(&mx_mn, io.cur, batch, m, n, io.ldc, io.cur_bs, 64, kBK))) return rc;
+  if ((rc = make_map(&ma, w.A, batch, m, m, w.ldm, w.ms, kBK, kBM))) return rc;
+  if ((rc = make_map(&mbm, w.B, batch, m, m, w.ldm, w.ms, kBK, kBM))) return rc;
+
+  GemmArgs base{};
+  base.M = int(m);
+  base.partial = w.splitk;
+  base.counters = w.counters;
+  base.tiles_m = P.tiles_m3;
+  base.tiles_n = P.tiles_n3;
 
   // GEMM1: A = X·Xᵀ
-  GemmArgs g1{};
-  g1.M = int(m); g1.N = int(m); g1.K = int(n);
-  g1.out = w.A; g1.ld_out = w.ldm;
-  if (pairs) {
-    g1.num_tiles = syrk_pair_tile_count(int(m));
-    rc = launch_gemm_pair<kSyrk>(ds, mx_k, mx_k, g1, st);
-  } else {
-    g1.num_tiles = syrk_tile_count(int(m));
-    rc = launch_gemm<kSyrk>(ds, mx_k, mx_k, g1, st);
-  }
-  if (rc) return rc;
+  GemmArgs g1 = base;
+  g1.N = int(m); g1.K = int(n);
+  g1.out = w.A; g1.ld_out = w.ldm; g1.bs_out = w.ms;
+  if ((rc = run_gemm<kSyrk>(ds, P, P.g[0], batch, mx_k, mx_k, g1, st))) return rc;
 
   // GEMM2: Boff = offdiag(c·A·A + b·A), diag = a + diag(c·A·A + b·A)
-  GemmArgs g2{};
-  g2.M = int(m); g2.N = int(m); g2.K = int(m);
-  g2.out = w.B; g2.ld_out = w.ldm;
-  g2.aux = w.A; g2.ld_aux = w.ldm;
-  g2.diag = w.diag;
-  if (pairs) {
-    g2.num_tiles = syrk_pair_tile_count(int(m));
-    rc = launch_gemm_pair<kPoly>(ds, ma, ma, g2, st);
-  } else {
-    g2.num_tiles = syrk_tile_count(int(m));
-    rc = launch_gemm<kPoly>(ds, ma, ma, g2, st);
-  }
-  if (rc) return rc;
+  GemmArgs g2 = base;
+  g2.N = int(m); g2.K = int(m);
+  g2.out = w.B; g2.ld_out = w.ldm; g2.bs_out = w.ms;
+  g2.aux = w.A; g2.ld_aux = w.ldm; g2.bs_aux = w.ms;
+  g2.diag = w.diag; g2.bs_diag = w.dsz;
+  if ((rc = run_gemm<kPoly>(ds, P, P.g[1], batch, ma, ma, g2, st))) return rc;
 
   // GEMM3: X' = diag ⊙ X + Boff·X
-  GemmArgs g3{};
-  g3.M = int(m); g3.N = int(n); g3.K = int(m);
-  g3.out = nxt; g3.ld_out = out_ld; g3.transpose_out = transpose_out;
-  g3.aux = cur; g3.ld_aux = ldc;
-  g3.diag = w.diag;
-  const int bm = pairs ? kPairBM : kBM, bn = pairs ? kPairBN : kBN;
-  g3.tiles_n = int((n + bn - 1) / bn);
-  g3.tiles_m = int((m + bm - 1) / bm);
-  g3.num_tiles = g3.tiles_m * g3.tiles_n;
-  return pairs ? launch_gemm_pair<kBX>(ds, mbm, mx_mn, g3, st)
-               : launch_gemm<kBX>(ds, mbm, mx_mn, g3, st);
+  GemmArgs g3 = base;
+  g3.N = int(n); g3.K = int(m);
+  g3.out = io.nxt; g3.ld_out = io.out_ld; g3.bs_out = io.out_bs;
+  g3.transpose_out = io.transpose_out;
+  g3.aux = io.cur; g3.ld_aux = io.ldc; g3.bs_aux = io.cur_bs;
+  g3.diag = w.diag; g3.bs_diag = w.dsz;
+  return run_gemm<kBX>(ds, P, P.g[2], batch, mbm, mx_mn, g3, st);
 }
 
 int check_dims(long long rows, long long cols) {
@@ -312,6 +397,73 @@ int prep_grid(long long rows, const DeviceState& ds) {
   return int(std::min<long long>(std::min<long long>(rows, kMaxPartials), ds.sm_count * 4));
 }
 
+// Full Newton-Schulz over a batch of same-shape matrices (batch = 1 for the
+// single-matrix entry points).
+int ns_run(const void* G, int dtype, long long batch, long long rows, long long cols, long long ldg,
+           long long bs_g, void* out, long long bs_out, int steps, void* workspace,
+           uint64_t workspace_bytes, cudaStream_t st) {
+  if (!G || !out || !workspace) return fail(FM_E_INVALID, "null pointer argument");
+  if (dtype < FM_DT_BF16 || dtype > FM_DT_F64) return fail(FM_E_INVALID, "unknown dtype %d", dtype);
+  if (steps < 0) return fail(FM_E_INVALID, "steps must be >= 0, got %d", steps);
+  if (batch < 1 || batch > 65535) return fail(FM_E_INVALID, "batch must be in [1, 65535], got %lld", batch);
+  if (int rc = check_dims(rows, cols)) return rc;
+  if (ldg < cols) return fail(FM_E_INVALID, "ldg %lld < cols %lld", ldg, cols);
+  if (batch > 1 && (bs_g < rows * ldg || bs_out < rows * cols))
+    return fail(FM_E_INVALID, "batch strides must not overlap matrices");
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
+    return fail(FM_E_INVALID, "workspace must be 256-byte aligned");
+  DeviceState* ds;
+  if (int rc = device_state(&ds)) return rc;
+  const bool tall = rows > cols;
+  const long long m = tall ? cols : rows, n = tall ? rows : cols;
+  Workspace w = layout(batch, m, n, workspace);
+  if (workspace_bytes < w.bytes)
+    return fail(FM_E_WORKSPACE, "workspace too small: need %zu bytes, got %llu", w.bytes,
+                (unsigned long long)workspace_bytes);
+  const NsPlan P = plan_ns(batch, m, n, g_gemm_path.load(std::memory_order_relaxed));
+  auto* o = static_cast<__nv_bfloat16*>(out);
+
+  const int pg = prep_grid(rows, *ds);
+  const long long tm = timer_begin(3, st);
+  if (P.split_slots > 0) FM_CUDA(cudaMemsetAsync(w.counters, 0, w.counter_bytes, st));
+  const long long bs_g_eff = batch > 1 ? bs_g : 0;
+  sumsq_kernel<<<dim3(pg, unsigned(batch)), kPrepThreads, 0, st>>>(
+      G, dtype, rows, cols, ldg, bs_g_eff, w.partials);
+  FM_CUDA(cudaGetLastError());
+  if (steps == 0) {  // normalised input, original orientation
+    scale_kernel<<<dim3(pg, unsigned(batch)), kPrepThreads, 0, st>>>(
+        G, dtype, rows, cols, ldg, bs_g_eff, w.partials, pg, o, cols, bs_out);
+    FM_CUDA(cudaGetLastError());
+    timer_end(tm, st);
+    return FM_OK;
+  }
+  if (tall) {
+    dim3 grid(unsigned((cols + kTT - 1) / kTT), unsigned((rows + kTT - 1) / kTT), unsigned(batch));
+    scale_transpose_kernel<<<grid, kPrepThreads, 0, st>>>(G, dtype, rows, cols, ldg, bs_g_eff,
+                                                          w.partials, pg, w.X[0], w.ldx, w.xs);
+  } else {
+    scale_kernel<<<dim3(pg, unsigned(batch)), kPrepThreads, 0, st>>>(
+        G, dtype, rows, cols, ldg, bs_g_eff, w.partials, pg, w.X[0], w.ldx, w.xs);
+  }
+  FM_CUDA(cudaGetLastError());
+  timer_end(tm, st);
+  for (int i = 0; i < steps; ++i) {
+    const bool last = i == steps - 1;
+    IterIO io;
+    io.cur = w.X[i & 1];
+    io.ldc = w.ldx;
+    io.cur_bs = w.xs;
+    // The last step writes the caller's output directly: row-major m x n, or
+    // its transpose (rows x cols = n x m) for tall inputs.
+    io.nxt = last ? o : w.X[(i + 1) & 1];
+    io.out_ld = last ? (tall ? m : n) : w.ldx;
+    io.out_bs = last ? bs_out : w.xs;
+    io.transpose_out = last && tall;
+    if (int rc = ns_iteration(*ds, w, P, batch, m, n, io, st)) return rc;
+  }
+  return FM_OK;
+}
+
 }  // namespace
 }  // namespace fm
 
@@ -323,64 +475,32 @@ int fm_version(void) { return 100; }
 
 const char* fm_last_error(void) { return t_err; }
 
-int fm_workspace_size(int64_t rows, int64_t cols, uint64_t* bytes) {
+int fm_workspace_size_batched(int64_t batch, int64_t rows, int64_t cols, uint64_t* bytes) {
   if (!bytes) return fail(FM_E_INVALID, "bytes is null");
+  if (batch < 1 || batch > 65535) return fail(FM_E_INVALID, "batch must be in [1, 65535], got %lld", (long long)batch);
   if (int rc = check_dims(rows, cols)) return rc;
   const long long m = std::min(rows, cols), n = std::max(rows, cols);
-  *bytes = layout(m, n, nullptr).bytes;
+  *bytes = layout(batch, m, n, nullptr).bytes;
   return FM_OK;
+}
+
+int fm_workspace_size(int64_t rows, int64_t cols, uint64_t* bytes) {
+  return fm_workspace_size_batched(1, rows, cols, bytes);
 }
 
 int fm_fused_newton_schulz(const void* G, int dtype, int64_t rows, int64_t cols, int64_t ldg,
                            void* out, int steps, void* workspace, uint64_t workspace_bytes,
                            void* stream) {
-  if (!G || !out || !workspace) return fail(FM_E_INVALID, "null pointer argument");
-  if (dtype < FM_DT_BF16 || dtype > FM_DT_F64) return fail(FM_E_INVALID, "unknown dtype %d", dtype);
-  if (steps < 0) return fail(FM_E_INVALID, "steps must be >= 0, got %d", steps);
-  if (int rc = check_dims(rows, cols)) return rc;
-  if (ldg < cols) return fail(FM_E_INVALID, "ldg %lld < cols %lld", (long long)ldg, (long long)cols);
-  if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0)
-    return fail(FM_E_INVALID, "workspace must be 256-byte aligned");
-  DeviceState* ds;
-  if (int rc = device_state(&ds)) return rc;
-  const bool tall = rows > cols;
-  const long long m = tall ? cols : rows, n = tall ? rows : cols;
-  Workspace w = layout(m, n, workspace);
-  if (workspace_bytes < w.bytes)
-    return fail(FM_E_WORKSPACE, "workspace too small: need %zu bytes, got %llu", w.bytes,
-                (unsigned long long)workspace_bytes);
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  auto* o = static_cast<__nv_bfloat16*>(out);
+  return ns_run(G, dtype, 1, rows, cols, ldg, 0, out, rows * cols, steps, workspace,
+                workspace_bytes, static_cast<cudaStream_t>(stream));
+}
 
-  const int pg = prep_grid(rows, *ds);
-  const long long tm = timer_begin(3, st);
-  sumsq_kernel<<<pg, kPrepThreads, 0, st>>>(G, dtype, rows, cols, ldg, w.partials);
-  FM_CUDA(cudaGetLastError());
-  if (steps == 0) {  // normalised input, original orientation
-    scale_kernel<<<pg, kPrepThreads, 0, st>>>(G, dtype, rows, cols, ldg, w.partials, pg, o, cols);
-    FM_CUDA(cudaGetLastError());
-    return FM_OK;
-  }
-  if (tall) {
-    dim3 grid(unsigned((cols + kTT - 1) / kTT), unsigned((rows + kTT - 1) / kTT));
-    scale_transpose_kernel<<<grid, kPrepThreads, 0, st>>>(G, dtype, rows, cols, ldg, w.partials,
-                                                          pg, w.X[0], w.ldx);
-  } else {
-    scale_kernel<<<pg, kPrepThreads, 0, st>>>(G, dtype, rows, cols, ldg, w.partials, pg, w.X[0],
-                                              w.ldx);
-  }
-  FM_CUDA(cudaGetLastError());
-  timer_end(tm, st);
-  for (int i = 0; i < steps; ++i) {
-    const __nv_bfloat16* cur = w.X[i & 1];
-    const bool last = i == steps - 1;
-    __nv_bfloat16* nxt = last ? o : w.X[(i + 1) & 1];
-    // Last step writes the caller's output directly: row-major m x n, or its
-    // transpose (rows x cols = n x m) for tall inputs.
-    const long long out_ld = last ? (tall ? m : n) : w.ldx;
-    if (int rc = ns_iteration(*ds, w, cur, w.ldx, m, n, nxt, out_ld, last && tall, st)) return rc;
-  }
-  return FM_OK;
+int fm_fused_newton_schulz_batched(const void* G, int dtype, int64_t batch, int64_t rows,
+                                   int64_t cols, int64_t ldg, int64_t batch_stride_g, void* out,
+                                   int64_t batch_stride_out, int steps, void* workspace,
+                                   uint64_t workspace_bytes, void* stream) {
+  return ns_run(G, dtype, batch, rows, cols, ldg, batch_stride_g, out, batch_stride_out, steps,
+                workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
 static int step_common(const void* X, int64_t m, int64_t n, int64_t ldx, void* X_new,
@@ -394,24 +514,33 @@ static int step_common(const void* X, int64_t m, int64_t n, int64_t ldx, void* X
   if (int rc = device_state(&ds)) return rc;
   // The layout is sized for (min, max); a step on a tall X needs the m x m
   // intermediates, so size it as m x max(m, n).
-  Workspace w = layout(m, std::max(m, n), workspace);
+  Workspace w = layout(1, m, std::max(m, n), workspace);
   if (workspace_bytes < w.bytes)
     return fail(FM_E_WORKSPACE, "workspace too small: need %zu bytes, got %llu", w.bytes,
                 (unsigned long long)workspace_bytes);
   w.ldx = round_up(n, 8);
+  w.xs = round_up(m * w.ldx, 128);
+  const NsPlan P = plan_ns(1, m, n, g_gemm_path.load(std::memory_order_relaxed));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const __nv_bfloat16* cur = static_cast<const __nv_bfloat16*>(X);
-  long long ldc = ldx;
+  if (P.split_slots > 0) FM_CUDA(cudaMemsetAsync(w.counters, 0, w.counter_bytes, st));
+  IterIO io;
+  io.cur = static_cast<const __nv_bfloat16*>(X);
+  io.ldc = ldx;
+  io.cur_bs = 0;
   if ((reinterpret_cast<uintptr_t>(X) & 15) != 0 || ldx % 8 != 0) {
     // Not TMA-addressable: copy into the workspace (no normalisation).
     const int pg = prep_grid(m, *ds);
-    scale_kernel<<<pg, kPrepThreads, 0, st>>>(X, FM_DT_BF16, m, n, ldx, nullptr, 0, w.X[0], w.ldx);
+    scale_kernel<<<dim3(pg, 1), kPrepThreads, 0, st>>>(X, FM_DT_BF16, m, n, ldx, 0, nullptr, 0,
+                                                      w.X[0], w.ldx, w.xs);
     FM_CUDA(cudaGetLastError());
-    cur = w.X[0];
-    ldc = w.ldx;
+    io.cur = w.X[0];
+    io.ldc = w.ldx;
   }
-  if (int rc = ns_iteration(*ds, w, cur, ldc, m, n, static_cast<__nv_bfloat16*>(X_new), n, 0, st))
-    return rc;
+  io.nxt = static_cast<__nv_bfloat16*>(X_new);
+  io.out_ld = n;
+  io.out_bs = m * n;
+  io.transpose_out = 0;
+  if (int rc = ns_iteration(*ds, w, P, 1, m, n, io, st)) return rc;
   *wout = w;
   return FM_OK;
 }
@@ -432,6 +561,74 @@ int fm_ns_step_debug(const void* X, int64_t m, int64_t n, int64_t ldx, void* A, 
   FM_CUDA(cudaMemcpy2DAsync(A, m * 2, w.A, w.ldm * 2, m * 2, m, cudaMemcpyDeviceToDevice, st));
   FM_CUDA(cudaMemcpy2DAsync(Boff, m * 2, w.B, w.ldm * 2, m * 2, m, cudaMemcpyDeviceToDevice, st));
   FM_CUDA(cudaMemcpyAsync(diag, w.diag, m * 4, cudaMemcpyDeviceToDevice, st));
+  return FM_OK;
+}
+
+namespace {
+int ew_grid(long long n, const DeviceState& ds) {
+  const long long blocks = (n + kEwThreads - 1) / kEwThreads;
+  return int(std::max<long long>(1, std::min<long long>(blocks, ds.sm_count * 8ll)));
+}
+}  // namespace
+
+int fm_muon_momentum(void* buf, const void* grad, void* dir, int64_t n, int dtype, float momentum,
+                     int nesterov, void* stream) {
+  if (!buf || !grad || !dir) return fail(FM_E_INVALID, "null pointer argument");
+  if (n < 0) return fail(FM_E_INVALID, "negative element count");
+  if (n == 0) return FM_OK;
+  DeviceState* ds;
+  if (int rc = device_state(&ds)) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  auto* d = static_cast<__nv_bfloat16*>(dir);
+  const int grid = ew_grid(n, *ds);
+  switch (dtype) {
+    case FM_DT_F32:
+      muon_momentum_bf16dir_kernel<float><<<grid, kEwThreads, 0, st>>>(
+          static_cast<float*>(buf), static_cast<const float*>(grad), d, n, momentum, nesterov);
+      break;
+    case FM_DT_BF16:
+      muon_momentum_bf16dir_kernel<__nv_bfloat16><<<grid, kEwThreads, 0, st>>>(
+          static_cast<__nv_bfloat16*>(buf), static_cast<const __nv_bfloat16*>(grad), d, n,
+          momentum, nesterov);
+      break;
+    case FM_DT_F16:
+      muon_momentum_bf16dir_kernel<__half><<<grid, kEwThreads, 0, st>>>(
+          static_cast<__half*>(buf), static_cast<const __half*>(grad), d, n, momentum, nesterov);
+      break;
+    default:
+      return fail(FM_E_INVALID, "fm_muon_momentum: unsupported dtype %d", dtype);
+  }
+  FM_CUDA(cudaGetLastError());
+  return FM_OK;
+}
+
+int fm_muon_apply(void* param, int dtype, const void* update, int64_t n, float decay, float alpha,
+                  void* stream) {
+  if (!param || !update) return fail(FM_E_INVALID, "null pointer argument");
+  if (n < 0) return fail(FM_E_INVALID, "negative element count");
+  if (n == 0) return FM_OK;
+  DeviceState* ds;
+  if (int rc = device_state(&ds)) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  auto* u = static_cast<const __nv_bfloat16*>(update);
+  const int grid = ew_grid(n, *ds);
+  switch (dtype) {
+    case FM_DT_F32:
+      muon_apply_kernel<float><<<grid, kEwThreads, 0, st>>>(static_cast<float*>(param), u, n, decay,
+                                                            alpha);
+      break;
+    case FM_DT_BF16:
+      muon_apply_kernel<__nv_bfloat16><<<grid, kEwThreads, 0, st>>>(
+          static_cast<__nv_bfloat16*>(param), u, n, decay, alpha);
+      break;
+    case FM_DT_F16:
+      muon_apply_kernel<__half><<<grid, kEwThreads, 0, st>>>(static_cast<__half*>(param), u, n,
+                                                             decay, alpha);
+      break;
+    default:
+      return fail(FM_E_INVALID, "fm_muon_apply: unsupported dtype %d", dtype);
+  }
+  FM_CUDA(cudaGetLastError());
   return FM_OK;
 }
 

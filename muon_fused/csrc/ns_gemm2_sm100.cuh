@@ -12,6 +12,12 @@
 //     both CTAs; "accumulator drained" is 4 local + 4 remote warp arrivals on
 //     the leader's barrier.
 // Six 32 KB stages (192 KB) keep about 3000 MMA cycles of loads in flight.
+//
+// Scheduling: a work unit is (matrix b of the batch, output tile, K-split s);
+// pairs walk the units persistently.  With split > 1 each split stashes its
+// fp32 accumulator half in the workspace; the last split to arrive (per tile
+// and CTA, counted with an atomic) sums all splits in split order — so the
+// result does not depend on arrival order — and runs the fused epilogue.
 #pragma once
 #include "ns_gemm_sm100.cuh"
 
@@ -42,6 +48,24 @@ __device__ __forceinline__ void pair_tile_coords(const GemmArgs& g, int t, int& 
     ti = i;
     tj = t - i * (i + 1) / 2;
   }
+}
+
+struct PairUnit {
+  int b, ti, tj, s, kb0, kb1, tile;
+};
+
+template <int MODE>
+__device__ __forceinline__ PairUnit pair_unit(const GemmArgs& g, int u, int num_kb) {
+  PairUnit w;
+  const int per_matrix = g.tiles * g.split;
+  w.b = u / per_matrix;
+  const int r = u - w.b * per_matrix;
+  w.tile = r / g.split;
+  w.s = r - w.tile * g.split;
+  pair_tile_coords<MODE>(g, w.tile, w.ti, w.tj);
+  w.kb0 = w.s * g.kb_per_split;
+  w.kb1 = (w.s == g.split - 1) ? num_kb : w.kb0 + g.kb_per_split;
+  return w;
 }
 
 template <int MODE>
@@ -97,11 +121,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       bool ok = true;
       for (int t = pair; t < g.num_tiles && ok; t += num_pairs) {
-        int ti, tj;
-        pair_tile_coords<MODE>(g, t, ti, tj);
-        const int arow = ti * kPairBM + static_cast<int>(rank) * 128;  // this CTA's A rows
-        const int bcol = tj * kPairBN + static_cast<int>(rank) * 128;  // this CTA's half of B
-        for (int kb = 0; kb < num_kb; ++kb) {
+        const PairUnit w = pair_unit<MODE>(g, t, num_kb);
+        const int arow = w.ti * kPairBM + static_cast<int>(rank) * 128;  // this CTA's A rows
+        const int bcol = w.tj * kPairBN + static_cast<int>(rank) * 128;  // this CTA's half of B
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag, g.err, kErrWaitEmpty)) {
             ok = false;
             break;
@@ -110,13 +133,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t fb = mapa_shared(smem_u32(&full_bar[stage]), 0);
           uint8_t* sa = smemA + stage * kPairTileA;
           uint8_t* sb = smemB + stage * kPairTileB;
-          tma_load_2d_pair(sa, &tmA, fb, kb * kBK, arow);
+          tma_load_3d_pair(sa, &tmA, fb, kb * kBK, arow, w.b);
           if constexpr (MODE == kBX) {
             // X columns bcol..bcol+127: two MN-major boxes of 64 columns x 64 rows
-            tma_load_2d_pair(sb, &tmB, fb, bcol, kb * kBK);
-            tma_load_2d_pair(sb + kBK * 64 * 2, &tmB, fb, bcol + 64, kb * kBK);
+            tma_load_3d_pair(sb, &tmB, fb, bcol, kb * kBK, w.b);
+            tma_load_3d_pair(sb + kBK * 64 * 2, &tmB, fb, bcol + 64, kb * kBK, w.b);
           } else {
-            tma_load_2d_pair(sb, &tmB, fb, kb * kBK, bcol);
+            tma_load_3d_pair(sb, &tmB, fb, kb * kBK, bcol, w.b);
           }
           if (++stage == kPairStages) {
             stage = 0;
@@ -141,8 +164,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after();
+        const PairUnit w = pair_unit<MODE>(g, t, num_kb);
         const uint32_t d_tmem = tmem_base + acc * kPairBN;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait_cluster(&full_bar[stage], phase, abort_flag, g.err, kErrWaitFull)) {
             ok = false;
             break;
@@ -159,7 +183,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             } else {
               bdesc = make_sdesc_sw128(sb + k * 32, 16, 1024);
             }
-            tc_mma_bf16_pair(d_tmem, adesc, bdesc, idesc, (kb | k) != 0 ? 1u : 0u);
+            tc_mma_bf16_pair(d_tmem, adesc, bdesc, idesc, (kb > w.kb0 || k > 0) ? 1u : 0u);
           }
           tc_commit_pair(&empty_bar[stage], 0x3);  // frees this stage in both CTAs
           if (++stage == kPairStages) {
@@ -180,16 +204,54 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;
     const bool out_vec = ((reinterpret_cast<uintptr_t>(g.out) | (g.ld_out * 2)) & 15) == 0;
     const bool aux_vec = ((reinterpret_cast<uintptr_t>(g.aux) | (g.ld_aux * 2)) & 15) == 0;
+    volatile int* last_flag = abort_flag + 1;  // smem word shared by the epilogue warps
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = pair; t < g.num_tiles; t += num_pairs) {
-      int ti, tj;
-      pair_tile_coords<MODE>(g, t, ti, tj);
-      const int row0w = ti * kPairBM + static_cast<int>(rank) * 128 + q * 32;
-      if (!epilogue_tile<MODE>(g, tmem_base + acc * kPairBN, q, row0w, tj * kPairBN, lane, out_vec,
-                               aux_vec, &accf_bar[acc], acc_phase, abort_flag))
-        break;
-      if (lane == 0) mbar_arrive_remote(mapa_shared(smem_u32(&acce_bar[acc]), 0));
+      const PairUnit w = pair_unit<MODE>(g, t, num_kb);
+      const GemmArgs gb = for_matrix(g, w.b);
+      const int row0w = w.ti * kPairBM + static_cast<int>(rank) * 128 + q * 32;
+      const int col0 = w.tj * kPairBN;
+      const uint32_t tacc = tmem_base + acc * kPairBN;
+      const uint32_t acce_remote = mapa_shared(smem_u32(&acce_bar[acc]), 0);
+      if (g.split == 1) {
+        if (!epilogue_tile<MODE>(gb, tacc, q, row0w, col0, lane, out_vec, aux_vec, &accf_bar[acc],
+                                 acc_phase, abort_flag))
+          break;
+        if (lane == 0) mbar_arrive_remote(acce_remote);
+      } else {
+        // this (matrix, tile, CTA half)'s partial slots, split 0 first
+        const long long slot = (static_cast<long long>(w.b) * g.tiles + w.tile) * 2 + rank;
+        float* parts = g.partial + slot * g.split * static_cast<long long>(kPartialFloats);
+        // A failed wait still goes through the three epilogue barriers below
+        // (so no warp is left waiting at one) and then leaves the loop.
+        const bool ok = stash_partial<MODE>(gb, tacc, q, row0w, col0, lane,
+                                            parts + static_cast<long long>(w.s) * kPartialFloats,
+                                            &accf_bar[acc], acc_phase, abort_flag);
+        if (ok && lane == 0) mbar_arrive_remote(acce_remote);  // TMEM free for the next unit
+        __threadfence();
+        epilogue_bar_sync();
+        if (threadIdx.x == 64) {  // first epilogue thread decides for all four warps
+          if (*abort_flag) {
+            *last_flag = 2;  // a wait failed (it raised the flag before the barrier)
+          } else {
+            const int prev = atomicAdd(&g.counters[slot], 1);
+            const int last = prev == g.split - 1;
+            if (last) g.counters[slot] = 0;  // ready for the next launch using this slot
+            *last_flag = last;
+          }
+        }
+        epilogue_bar_sync();
+        const int verdict = *last_flag;
+        epilogue_bar_sync();  // everyone has read the verdict before it is rewritten
+        if (verdict == 2) break;
+        const bool last = verdict == 1;
+        if (last) {
+          __threadfence();
+          epilogue_tile<MODE, true>(gb, 0, q, row0w, col0, lane, out_vec, aux_vec, nullptr, 0,
+                                    abort_flag, parts, g.split);
+        }
+      }
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1;

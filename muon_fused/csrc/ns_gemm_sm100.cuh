@@ -55,7 +55,7 @@ struct GemmArgs {
   int M;          // output rows (m)
   int N;          // output columns: m for kSyrk/kPoly, n for kBX
   int K;          // reduction length: n for kSyrk, m otherwise
-  int num_tiles;  // scheduled tiles
+  int num_tiles;  // scheduled work units (batch x tiles x split)
   int tiles_n;    // kBX: column tiles per row block
   int tiles_m;    // kBX: row tiles per column block
   __nv_bfloat16* out;
@@ -65,7 +65,25 @@ struct GemmArgs {
   float* diag;        // kPoly: written; kBX: read
   int transpose_out;  // kBX: store X'ᵀ (ld_out is then the row stride of X'ᵀ)
   unsigned* err;      // device error word
+  // Batched / split-K scheduling (CTA-pair kernel only; the single-CTA kernel
+  // requires batch == 1 and split == 1).
+  int batch;          // same-shape matrices in this launch (TMA dim 2 = matrix index)
+  int tiles;          // output tiles per matrix
+  int split;          // K-splits per tile
+  int kb_per_split;   // K-blocks per split; the last split takes the remainder
+  long long bs_out, bs_aux, bs_diag;  // per-matrix element strides
+  float* partial;     // split > 1: fp32 partial tiles, 128 KB per (unit, CTA)
+  int* counters;      // split > 1: arrivals per (matrix, tile, CTA), zero between uses
 };
+
+// A GemmArgs whose pointers address matrix b of the batch.
+__device__ __forceinline__ GemmArgs for_matrix(const GemmArgs& g, int b) {
+  GemmArgs r = g;
+  r.out = g.out + b * g.bs_out;
+  r.aux = g.aux ? g.aux + b * g.bs_aux : nullptr;
+  r.diag = g.diag ? g.diag + b * g.bs_diag : nullptr;
+  return r;
+}
 
 // Number of 128x256 tiles intersecting the lower triangle of an m x m matrix.
 __host__ __device__ inline int syrk_tile_count(int m) {
@@ -191,24 +209,64 @@ __device__ __forceinline__ void store_row32(__nv_bfloat16* rowp, int c0, int nco
   }
 }
 
-// Epilogue of one accumulator tile for one warp: TMEM lane quarter q holds
-// rows row0w .. row0w+31 of the output; the tile's columns start at col0 and
-// the accumulator's first TMEM column is tmem_acc.  Waits for the
-// accumulator on accf_bar (parity acc_phase), returns false if that wait
-// gave up.  Shared by the 1-CTA and the 2-CTA kernels.
+// Number of 32-column chunks of a tile row block that warp rows row0w.. store:
+// a prefix (columns below N; for the SYRK modes also at or left of the warp's
+// last row).
 template <int MODE>
+__device__ __forceinline__ int epilogue_chunks(const GemmArgs& g, int row0w, int col0) {
+  int col_end = min(g.N, col0 + kBN);
+  if constexpr (MODE != kBX) col_end = min(col_end, row0w + 32);
+  return row0w < g.M ? max(0, (col_end - col0 + 31) / 32) : 0;
+}
+
+// Split-K partial layout for one CTA's 128 x 256 fp32 accumulator:
+// element (row 32q + lane, column 32c + k) at ((q*8 + c)*32 + k)*32 + lane,
+// so each warp store / load instruction covers 128 contiguous bytes.
+constexpr int kPartialFloats = 128 * 256;
+__device__ __forceinline__ int partial_index(int q, int c, int k, int lane) {
+  return ((q * 8 + c) * 32 + k) * 32 + lane;
+}
+
+// Split-K, first half of the epilogue: wait for this split's accumulator and
+// write its needed chunks to `dst` (this unit's partial slot).  Returns false
+// if the wait gave up.
+template <int MODE>
+__device__ __forceinline__ bool stash_partial(const GemmArgs& g, uint32_t tmem_acc, int q, int row0w,
+                                              int col0, int lane, float* dst, uint64_t* accf_bar,
+                                              uint32_t acc_phase, volatile int* abort_flag) {
+  const int nc = epilogue_chunks<MODE>(g, row0w, col0);
+  if (!mbar_wait(accf_bar, acc_phase, abort_flag, g.err, kErrWaitAccFull)) return false;
+  tc_fence_after();
+#pragma unroll 1
+  for (int c = 0; c < nc; ++c) {
+    float v[32];
+    tmem_ld_32x32b_x32(tmem_acc + c * 32 + (static_cast<uint32_t>(q * 32) << 16), v);
+#pragma unroll
+    for (int k = 0; k < 32; ++k) __stcg(dst + partial_index(q, c, k, lane), v[k]);
+  }
+  tc_fence_before();
+  __syncwarp();
+  return true;
+}
+
+// Epilogue of one output tile for one warp: lane quarter q holds rows
+// row0w .. row0w+31; the tile's columns start at col0.
+//   FROM_PARTIALS = false: values come from the TMEM accumulator at tmem_acc,
+//     after waiting on accf_bar (parity acc_phase); returns false if that
+//     wait gave up.  Shared by the 1-CTA and the 2-CTA kernels.
+//   FROM_PARTIALS = true: values are the sum, in split order, of `split`
+//     fp32 partials starting at `parts` (stride kPartialFloats) — the
+//     last-arriving split of a split-K tile runs this.
+template <int MODE, bool FROM_PARTIALS = false>
 __device__ __forceinline__ bool epilogue_tile(const GemmArgs& g, uint32_t tmem_acc, int q,
                                               int row0w, int col0, int lane, bool out_vec,
                                               bool aux_vec, uint64_t* accf_bar, uint32_t acc_phase,
-                                              volatile int* abort_flag) {
+                                              volatile int* abort_flag,
+                                              const float* parts = nullptr, int split = 1) {
   const int row = row0w + lane;
   const bool row_ok = row < g.M;
   const __nv_bfloat16* aux_row = g.aux + static_cast<long long>(row) * g.ld_aux;
-  // Chunks of 32 columns this warp stores: a prefix 0..nc-1 (columns below N;
-  // for the SYRK modes also at or left of the warp's last row).
-  int col_end = min(g.N, col0 + kBN);
-  if constexpr (MODE != kBX) col_end = min(col_end, row0w + 32);
-  const int nc = row0w < g.M ? max(0, (col_end - col0 + 31) / 32) : 0;
+  const int nc = epilogue_chunks<MODE>(g, row0w, col0);
   // The epilogue operand (A for kPoly, X for kBX) does not depend on the
   // accumulator: fetch the first chunk before waiting for the MMAs and each
   // next chunk while the current one is processed.
@@ -218,8 +276,10 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& g, uint32_t tmem_a
   }
   float dval = 0.f;
   if constexpr (MODE == kBX) dval = row_ok ? g.diag[row] : 0.f;
-  if (!mbar_wait(accf_bar, acc_phase, abort_flag, g.err, kErrWaitAccFull)) return false;
-  tc_fence_after();
+  if constexpr (!FROM_PARTIALS) {
+    if (!mbar_wait(accf_bar, acc_phase, abort_flag, g.err, kErrWaitAccFull)) return false;
+    tc_fence_after();
+  }
 #pragma unroll 1
   for (int c = 0; c < nc; ++c) {
     const int c0 = col0 + c * 32;
@@ -227,7 +287,17 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& g, uint32_t tmem_a
       if (c + 1 < nc && row_ok) load_raw32(aux_row, c0 + 32, g.N, aux_vec, anext);
     }
     float v[32];
-    tmem_ld_32x32b_x32(tmem_acc + c * 32 + (static_cast<uint32_t>(q * 32) << 16), v);
+    if constexpr (FROM_PARTIALS) {
+#pragma unroll
+      for (int k = 0; k < 32; ++k) v[k] = __ldcg(parts + partial_index(q, c, k, lane));
+      for (int sp = 1; sp < split; ++sp) {
+        const float* ps = parts + static_cast<long long>(sp) * kPartialFloats;
+#pragma unroll
+        for (int k = 0; k < 32; ++k) v[k] += __ldcg(ps + partial_index(q, c, k, lane));
+      }
+    } else {
+      tmem_ld_32x32b_x32(tmem_acc + c * 32 + (static_cast<uint32_t>(q * 32) << 16), v);
+    }
     if (row_ok) {
       if constexpr (MODE == kSyrk) {
         store_row32(g.out + row * g.ld_out, c0, g.N, row, true, out_vec, v);
@@ -270,7 +340,7 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& g, uint32_t tmem_a
       for (int k = 0; k < 4; ++k) araw[k] = anext[k];
     }
   }
-  tc_fence_before();
+  if constexpr (!FROM_PARTIALS) tc_fence_before();
   __syncwarp();
   return true;
 }
@@ -336,17 +406,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive_expect_tx(&full_bar[stage], kStageBytes);
           uint8_t* sa = smemA + stage * kTileABytes;
           uint8_t* sb = smemB + stage * kTileBBytes;
-          tma_load_2d(sa, &tmA, &full_bar[stage], kb * kBK, ti * kBM);
+          tma_load_3d(sa, &tmA, &full_bar[stage], kb * kBK, ti * kBM, 0);
           if constexpr (MODE == kBX) {
             // B operand is X (K = rows, N = contiguous columns): four MN-major
             // boxes of 64 columns x 64 rows, 8 KB apart.
 #pragma unroll
             for (int q = 0; q < 4; ++q)
-              tma_load_2d(sb + q * (kBK * 64 * 2), &tmB, &full_bar[stage], tj * kBN + q * 64,
-                          kb * kBK);
+              tma_load_3d(sb + q * (kBK * 64 * 2), &tmB, &full_bar[stage], tj * kBN + q * 64,
+                          kb * kBK, 0);
           } else {
-            tma_load_2d(sb, &tmB, &full_bar[stage], kb * kBK, tj * kBN);
-            tma_load_2d(sb + kTileABytes, &tmB, &full_bar[stage], kb * kBK, tj * kBN + kBM);
+            tma_load_3d(sb, &tmB, &full_bar[stage], kb * kBK, tj * kBN, 0);
+            tma_load_3d(sb + kTileABytes, &tmB, &full_bar[stage], kb * kBK, tj * kBN + kBM, 0);
           }
           if (++stage == kStages) {
             stage = 0;

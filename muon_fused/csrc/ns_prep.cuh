@@ -90,14 +90,24 @@ __device__ __forceinline__ void load_chunk(const void* G, int dtype, const Chunk
   }
 }
 
+// Matrix b of a batch: element offset b * bs of an input of the given dtype.
+__device__ __forceinline__ const void* batch_ptr(const void* G, int dtype, long long bs, int b) {
+  const size_t esz = dtype == kDtF32 ? 4 : dtype == kDtF64 ? 8 : 2;
+  return static_cast<const char*>(G) + static_cast<long long>(b) * bs * esz;
+}
+
 __device__ __forceinline__ bool bf16_vec_ok(const void* p, int dtype, long long ld) {
   return dtype == kDtBF16 && ((reinterpret_cast<uintptr_t>(p) | static_cast<uintptr_t>(ld * 2)) & 15) == 0;
 }
 
-// partials[blockIdx.x] = sum over this block's rows of bf16(G)^2 (fp32).
-__global__ void __launch_bounds__(kPrepThreads) sumsq_kernel(const void* __restrict__ G, int dtype,
+// partials[b][blockIdx.x] = sum over this block's rows of bf16(G_b)^2 (fp32);
+// blockIdx.y = b, the matrix of the batch (element stride bs_g).
+__global__ void __launch_bounds__(kPrepThreads) sumsq_kernel(const void* __restrict__ G0, int dtype,
                                                              long long rows, long long cols,
-                                                             long long ldg, float* partials) {
+                                                             long long ldg, long long bs_g,
+                                                             float* partials) {
+  const void* G = batch_ptr(G0, dtype, bs_g, blockIdx.y);
+  partials += static_cast<long long>(blockIdx.y) * kMaxPartials;
   const ChunkGrid g{rows, cols, ldg, (cols + 7) / 8};
   const bool vec = bf16_vec_ok(G, dtype, ldg);
   long long r0, r1;
@@ -145,13 +155,18 @@ __device__ __forceinline__ float norm_denominator(const float* partials, int npa
   return *shared_slot;
 }
 
-// X[r][c] = bf16(bf16(G[r][c]) / (||G|| + 1e-7)), same layout as G.
+// X[r][c] = bf16(bf16(G[r][c]) / (||G|| + 1e-7)), same layout as G;
+// blockIdx.y = matrix of the batch (element strides bs_g in, xs out).
 // With nparts == 0 no normalisation is applied (plain cast/copy).
-__global__ void __launch_bounds__(kPrepThreads) scale_kernel(const void* __restrict__ G, int dtype,
+__global__ void __launch_bounds__(kPrepThreads) scale_kernel(const void* __restrict__ G0, int dtype,
                                                              long long rows, long long cols,
-                                                             long long ldg, const float* partials,
-                                                             int nparts, __nv_bfloat16* X,
-                                                             long long ldx) {
+                                                             long long ldg, long long bs_g,
+                                                             const float* partials, int nparts,
+                                                             __nv_bfloat16* X, long long ldx,
+                                                             long long xs) {
+  const void* G = batch_ptr(G0, dtype, bs_g, blockIdx.y);
+  if (partials) partials += static_cast<long long>(blockIdx.y) * kMaxPartials;
+  X += static_cast<long long>(blockIdx.y) * xs;
   __shared__ float s_den;
   const float den = nparts > 0 ? norm_denominator(partials, nparts, &s_den) : 1.f;
   const ChunkGrid g{rows, cols, ldg, (cols + 7) / 8};
@@ -190,8 +205,12 @@ __global__ void __launch_bounds__(kPrepThreads) scale_kernel(const void* __restr
 // 64x64 tiles through shared memory so both the read and the write coalesce.
 constexpr int kTT = 64;
 __global__ void __launch_bounds__(kPrepThreads) scale_transpose_kernel(
-    const void* __restrict__ G, int dtype, long long rows, long long cols, long long ldg,
-    const float* partials, int nparts, __nv_bfloat16* X, long long ldx) {
+    const void* __restrict__ G0, int dtype, long long rows, long long cols, long long ldg,
+    long long bs_g, const float* partials, int nparts, __nv_bfloat16* X, long long ldx,
+    long long xs) {
+  const void* G = batch_ptr(G0, dtype, bs_g, blockIdx.z);
+  partials += static_cast<long long>(blockIdx.z) * kMaxPartials;
+  X += static_cast<long long>(blockIdx.z) * xs;
   __shared__ float s_den;
   __shared__ __align__(16) __nv_bfloat16 tile[kTT][kTT + 8];
   const float den = nparts > 0 ? norm_denominator(partials, nparts, &s_den) : 1.f;

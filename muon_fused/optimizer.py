@@ -28,7 +28,19 @@ from typing import Any
 import torch
 from torch.optim import Optimizer
 
-from muon_fused.ns_step import fused_newton_schulz, workspace_size
+from muon_fused import _fused_muon_C as _C
+from muon_fused import _lib
+from muon_fused.ns_step import workspace_size
+
+# Parameter / gradient dtypes the fused elementwise kernels handle.
+_EW_DTYPES = {torch.float32: _lib.FM_DT_F32, torch.bfloat16: _lib.FM_DT_BF16,
+              torch.float16: _lib.FM_DT_F16}
+
+
+def _ns_batched(G: torch.Tensor, steps: int, workspace: torch.Tensor, out: torch.Tensor):
+    """Batched Newton-Schulz used by the optimizer (module level so a test can
+    substitute a CPU implementation in a gloo child process)."""
+    return _C.fused_newton_schulz_batched(G, steps, workspace, out=out)
 
 
 class FusedMuon(Optimizer):
@@ -48,6 +60,9 @@ class FusedMuon(Optimizer):
             the world group when ``torch.distributed`` is initialised.
         bucket_bytes: size of each all-gather bucket of packed updates when
             sharded (default 256 MiB).
+        batch_bytes: device memory one batched Newton-Schulz call may use for
+            its inputs, outputs and workspace (default 4 GiB); same-shape
+            matrices are batched up to this budget.
     """
 
     def __init__(
@@ -62,6 +77,7 @@ class FusedMuon(Optimizer):
         adamw_eps: float = 1e-8,
         process_group=None,
         bucket_bytes: int = 256 << 20,
+        batch_bytes: int = 4 << 30,
     ):
         defaults: dict[str, Any] = dict(
             lr=lr, wd=wd, momentum=momentum, nesterov=nesterov, ns_steps=ns_steps,
@@ -71,7 +87,9 @@ class FusedMuon(Optimizer):
         self._workspaces: dict[tuple, torch.Tensor] = {}
         self._process_group = process_group
         self._bucket_bytes = int(bucket_bytes)
+        self._batch_bytes = int(batch_bytes)
         self._plans: dict[tuple, Any] = {}
+        self._arena: dict[torch.device, torch.Tensor] = {}
 
     # ------------------------------------------------------------------ helpers
     @staticmethod
@@ -98,38 +116,110 @@ class FusedMuon(Optimizer):
         return pg, dist.get_rank(pg), dist.get_world_size(pg)
 
     # ------------------------------------------------------------------ Muon
-    def _momentum_direction(self, p: torch.Tensor, g: torch.Tensor, momentum: float,
-                            nesterov: bool) -> torch.Tensor:
-        """buf ← μ·buf + g; returns g + μ·buf (nesterov) or buf (optimizer.py:139-149)."""
+    def _momentum_into(self, p: torch.Tensor, g: torch.Tensor, dst: torch.Tensor, momentum: float,
+                       nesterov: bool) -> None:
+        """buf ← μ·buf + g; dst ← bf16(g + μ·buf) (nesterov) or bf16(buf)
+        (optimizer.py:139-149).
+
+        On CUDA this is one fused kernel (fm_muon_momentum) writing the bf16
+        Newton-Schulz input straight into ``dst``; the buffer is bit-identical
+        to the reference's torch ops.  CPU tensors (no Newton-Schulz path
+        exists for them) keep the reference's torch ops."""
         state = self.state[p]
         if "momentum_buffer" not in state:
             state["momentum_buffer"] = torch.zeros_like(g)
         buf = state["momentum_buffer"]
+        dt = _EW_DTYPES.get(g.dtype)
+        if g.is_cuda and dt is not None and buf.is_contiguous() and dst.is_contiguous():
+            gc = g if g.is_contiguous() else g.contiguous()
+            with torch.cuda.device(g.device):
+                _lib.check(_lib.load().fm_muon_momentum(
+                    buf.data_ptr(), gc.data_ptr(), dst.data_ptr(), g.numel(), dt,
+                    float(momentum), 1 if nesterov else 0,
+                    torch.cuda.current_stream(g.device).cuda_stream), "fm_muon_momentum")
+            return
         buf.mul_(momentum).add_(g)
-        return g.add(buf, alpha=momentum) if nesterov else buf
+        dst.copy_(g.add(buf, alpha=momentum) if nesterov else buf)
 
-    def _orthogonalise(self, p: torch.Tensor, group) -> torch.Tensor:
-        g = p.grad
-        if g.ndim > 2:
-            g = g.view(g.size(0), -1)
-        d = self._momentum_direction(p, g, group["momentum"], group["nesterov"])
-        ws = self._get_workspace(d.size(0), d.size(1), d.device)
-        return fused_newton_schulz(d, steps=group["ns_steps"], workspace=ws)
+    def _scratch(self, device: torch.device, nbytes: int) -> torch.Tensor:
+        """One reusable device buffer per device for batch inputs, outputs and
+        the Newton-Schulz workspace.  Reuse is safe because every user is
+        ordered on the same stream."""
+        buf = self._arena.get(device)
+        if buf is None or buf.numel() < nbytes:
+            buf = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=device)
+            self._arena[device] = buf
+        return buf
+
+    def _batch_limit(self, rows: int, cols: int) -> int:
+        """Matrices per batched call so inputs, outputs and workspace of one
+        batch stay within ``batch_bytes``."""
+        per = _C.workspace_size_batched(1, rows, cols) + 4 * rows * cols
+        return max(1, min(64, self._batch_bytes // per))
+
+    def _orthogonalise_batch(self, params, group, out=None) -> torch.Tensor:
+        """Momentum + Newton-Schulz for same-shape parameters in one batched
+        call; returns (B, rows, cols) bf16 updates (written into ``out`` when
+        given, e.g. a slice of the all-gather send buffer)."""
+        g0 = params[0].grad
+        rows = g0.size(0)
+        cols = g0.numel() // rows
+        B = len(params)
+        dev = g0.device
+        n_el = B * rows * cols
+        dir_bytes = (2 * n_el + 255) // 256 * 256
+        ws_bytes = _C.workspace_size_batched(B, rows, cols)
+        out_bytes = 0 if out is not None else (2 * n_el + 255) // 256 * 256
+        arena = self._scratch(dev, dir_bytes + out_bytes + ws_bytes)
+        dirs = arena[:2 * n_el].view(torch.bfloat16).view(B, rows, cols)
+        if out is None:
+            out = arena[dir_bytes:dir_bytes + 2 * n_el].view(torch.bfloat16).view(B, rows, cols)
+        ws = arena[dir_bytes + out_bytes:dir_bytes + out_bytes + ws_bytes]
+        for b, p in enumerate(params):
+            g = p.grad
+            if g.ndim > 2:
+                g = g.view(g.size(0), -1)
+            self._momentum_into(p, g, dirs[b], group["momentum"], group["nesterov"])
+        _ns_batched(dirs, group["ns_steps"], ws, out)
+        return out
 
     @staticmethod
     def _apply_update(p: torch.Tensor, u: torch.Tensor, lr: float, wd: float) -> None:
-        """p ← p·(1 − lr·wd) − lr'·u (optimizer.py:157-163)."""
+        """p ← p·(1 − lr·wd) − lr'·u (optimizer.py:157-163), one fused pass
+        (fm_muon_apply) on CUDA, bit-identical to the two torch ops."""
         if u.shape != p.shape:
             u = u.view_as(p)
-        p.data.mul_(1 - lr * wd)
-        p.data.add_(u, alpha=-FusedMuon.adjust_lr_for_muon(lr, p.shape))
+        alpha = -FusedMuon.adjust_lr_for_muon(lr, p.shape)
+        dt = _EW_DTYPES.get(p.dtype)
+        data = p.data
+        if (data.is_cuda and dt is not None and data.is_contiguous() and u.is_contiguous()
+                and u.dtype == torch.bfloat16):
+            with torch.cuda.device(data.device):
+                _lib.check(_lib.load().fm_muon_apply(
+                    data.data_ptr(), dt, u.data_ptr(), data.numel(), float(1 - lr * wd),
+                    float(alpha), torch.cuda.current_stream(data.device).cuda_stream),
+                    "fm_muon_apply")
+            return
+        data.mul_(1 - lr * wd)
+        data.add_(u, alpha=alpha)
 
     def _muon_group_local(self, group) -> None:
+        """All matrices on this process: same-shape parameters are batched
+        into one Newton-Schulz call (the reference loops one matrix at a time,
+        optimizer.py:128-163)."""
+        by_shape: dict[tuple, list] = {}
         for p in group["params"]:
             if p.grad is None:
                 continue
-            u = self._orthogonalise(p, group)
-            self._apply_update(p, u, group["lr"], group["wd"])
+            key = (p.grad.device, p.shape[0], p.grad.numel() // p.shape[0])
+            by_shape.setdefault(key, []).append(p)
+        for (_, rows, cols), plist in by_shape.items():
+            lim = self._batch_limit(rows, cols)
+            for k in range(0, len(plist), lim):
+                chunk = plist[k:k + lim]
+                out = self._orthogonalise_batch(chunk, group)
+                for b, p in enumerate(chunk):
+                    self._apply_update(p, out[b], group["lr"], group["wd"])
 
     def _muon_group_sharded(self, group, pg, rank: int, world: int) -> None:
         from muon_fused import sharding
@@ -144,8 +234,12 @@ class FusedMuon(Optimizer):
                                             self._bucket_bytes)
             self._plans[key] = plan
 
-        def compute(i: int) -> torch.Tensor:
-            return self._orthogonalise(params[i], group)
+        def compute(indices, out) -> None:
+            rows, cols = out.shape[1], out.shape[2]
+            lim = self._batch_limit(rows, cols)
+            for k in range(0, len(indices), lim):
+                self._orthogonalise_batch([params[i] for i in indices[k:k + lim]], group,
+                                          out[k:k + lim])
 
         def apply(i: int, u: torch.Tensor) -> None:
             self._apply_update(params[i], u, group["lr"], group["wd"])

@@ -76,8 +76,9 @@ class ShardPlan:
         per_rank_chunks: list[list[list[tuple[int, int]]]] = []
         for r in range(world):
             mine = [i for i in range(len(shapes)) if owner[i] == r]
-            # heaviest first, so the first buckets carry the long Newton-Schulz calls
-            mine.sort(key=lambda i: (-ns_flops(shapes[i]), i))
+            # heaviest first, so the first buckets carry the long Newton-Schulz
+            # calls; equal shapes adjacent so they pack into one batched call
+            mine.sort(key=lambda i: (-ns_flops(shapes[i]), shapes[i], i))
             chunks, cur, used = [], [], 0
             for i in mine:
                 sz = numel(shapes[i])
@@ -114,9 +115,11 @@ def _all_gather(out: torch.Tensor, inp: torch.Tensor, pg, world: int):
 def run_sharded(plan: ShardPlan, rank: int, pg, device, compute, apply) -> None:
     """Execute one sharded step.
 
-    ``compute(i) -> Tensor`` returns matrix i's bf16 update (called only on
-    the owner); ``apply(i, u)`` applies an update to parameter i (called on
-    every rank, in matrix order within each bucket).
+    ``compute(indices, out)`` writes the bf16 updates of the same-shape
+    matrices ``indices`` (owned by this rank, packed back to back in the send
+    buffer) into ``out``, a (len(indices), rows, cols) view of that buffer;
+    ``apply(i, u)`` applies an update to parameter i (called on every rank,
+    in matrix order within each bucket).
     """
     world = plan.world
     pending = []
@@ -124,10 +127,25 @@ def run_sharded(plan: ShardPlan, rank: int, pg, device, compute, apply) -> None:
         size = plan.bucket_numel[k]
         if size == 0:
             continue
-        send = torch.zeros(size, dtype=torch.bfloat16, device=device)
-        for i, off in row[rank]:
-            u = compute(i)
-            send[off:off + u.numel()].copy_(u.reshape(-1))
+        send = torch.empty(size, dtype=torch.bfloat16, device=device)
+        mine = row[rank]
+        j = 0
+        while j < len(mine):
+            # a run of consecutive same-shape matrices is one batched call
+            i0, off0 = mine[j]
+            shape = plan.shapes[i0]
+            e = j + 1
+            while e < len(mine) and plan.shapes[mine[e][0]] == shape:
+                e += 1
+            rows = shape[0]
+            cols = numel(shape) // rows
+            n = e - j
+            out = send[off0:off0 + n * rows * cols].view(n, rows, cols)
+            compute([i for i, _ in mine[j:e]], out)
+            j = e
+        used = max((off + numel(plan.shapes[i]) for i, off in mine[-1:]), default=0)
+        if used < size:
+            send[used:].zero_()  # padding up to the largest rank's share
         recv = torch.empty(world * size, dtype=torch.bfloat16, device=device)
         work = _all_gather(recv, send, pg, world)
         pending.append((k, recv, work, send))

@@ -1,0 +1,181 @@
+"""FusedMuon on the GPU against the oracle's restatement of the reference
+optimizer (muon_fused/optimizer.py:99-202, benchmarks/reference_muon.py:94-154).
+
+Unlike the reference's own tests/test_optimizer.py (which passes plain
+parameter lists, so both optimizers silently run AdamW, optimizer.py:116),
+these tests put the matrices in ``use_muon=True`` groups.
+"""
+
+import copy
+
+import pytest
+import torch
+
+from oracle import ns_oracle as O
+from tests.golden.make_golden import muon_grads
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def _groups(params, hp):
+    return [
+        {"params": params[:3], "use_muon": True},
+        {"params": params[3:], "use_muon": False},
+    ]
+
+
+def test_matches_reference_golden(cuda_lib, golden):
+    """Three steps on the golden parameter set: Muon deltas within 4e-2 of the
+    reference's (its bf16 NS is itself ~3e-2 from fp32), momentum buffers
+    bit-identical, AdamW parameters equal to fp32 rounding."""
+    from muon_fused import FusedMuon
+
+    g = golden["muon"]
+    hp = g["hp"]
+    params = [torch.nn.Parameter(p.clone().to(DEV)) for p in g["init"]]
+    opt = FusedMuon(_groups(params, hp), lr=hp["lr"], wd=hp["wd"], momentum=hp["momentum"],
+                    nesterov=hp["nesterov"], ns_steps=hp["ns_steps"])
+    for s in range(g["steps"]):
+        for p, gr in zip(params, muon_grads(g["init"], s)):
+            p.grad = gr.to(DEV)
+        opt.step()
+    torch.cuda.synchronize()
+    for i in range(3):
+        got = params[i].detach().cpu()
+        d_got = got - g["init"][i]
+        d_ref = g["final"][i] - g["init"][i]
+        assert O.rel_fro(d_got, d_ref) < 4e-2, i
+        assert torch.equal(opt.state[params[i]]["momentum_buffer"].cpu(), g["momentum"][i])
+    torch.testing.assert_close(params[3].detach().cpu(), g["final"][3], rtol=1e-6, atol=1e-8)
+
+
+def test_matches_oracle_fp32_ns(cuda_lib):
+    """Same step with the oracle driven by the fp32 Newton-Schulz: the only
+    remaining difference is our bf16 NS (<= 1e-2 of fp32), so the deltas
+    agree to 1e-2."""
+    from muon_fused import FusedMuon
+
+    torch.manual_seed(0)
+    shapes = [(256, 512), (512, 256), (384, 384), (64, 16, 3, 3)]
+    init = [torch.randn(s) * 0.02 for s in shapes]
+    gpu = [torch.nn.Parameter(p.clone().to(DEV)) for p in init]
+    cpu = [p.clone() for p in init]
+    opt = FusedMuon([{"params": gpu, "use_muon": True}], lr=0.02, momentum=0.95)
+    groups = [dict(params=cpu, use_muon=True, lr=0.02, wd=0.1, momentum=0.95, nesterov=True,
+                   ns_steps=5)]
+    state = {}
+    for step in range(3):
+        gen = torch.Generator().manual_seed(100 + step)
+        grads = [torch.randn(s, generator=gen) * 1e-3 for s in shapes]
+        for p, gr in zip(gpu, grads):
+            p.grad = gr.to(DEV)
+        for p, gr in zip(cpu, grads):
+            p.grad = gr.clone()
+        opt.step()
+        O.muon_reference_step(groups, state, ns=O.ns_fp32)
+    torch.cuda.synchronize()
+    for a, b, p0 in zip(gpu, cpu, init):
+        assert O.rel_fro(a.detach().cpu() - p0, b - p0) < 1e-2
+
+
+def test_reference_mlp_pattern_with_muon_groups(cuda_lib):
+    """The reference's MLP integration test (tests/test_optimizer.py:63-131):
+    128->256->128 bias-free MLP, 5 steps — here with the matrices actually in
+    a Muon group.  The reference's elementwise relative-error gate only held
+    because both of its optimizers ran the identical AdamW code; with real
+    Muon updates some weights cross zero, so the 5% gate is applied to the
+    Frobenius-relative difference of the accumulated parameter change.  The
+    oracle runs the fp32 Newton-Schulz: over five steps of a real training
+    loop, the reference's own bf16 NS (~3e-2 per call from fp32) drifts by
+    ~1e-1 in parameter change from any more accurate implementation."""
+    from muon_fused import FusedMuon
+
+    torch.manual_seed(0)
+    model = torch.nn.Sequential(torch.nn.Linear(128, 256, bias=False), torch.nn.ReLU(),
+                                torch.nn.Linear(256, 128, bias=False))
+    model_gpu = copy.deepcopy(model).to(DEV)
+    pg = [p for p in model_gpu.parameters() if p.ndim == 2]
+    pc = [p for p in model.parameters() if p.ndim == 2]
+    opt = FusedMuon([{"params": pg, "use_muon": True}], lr=0.02, momentum=0.95)
+    groups = [dict(params=pc, use_muon=True, lr=0.02, wd=0.1, momentum=0.95, nesterov=True,
+                   ns_steps=5)]
+    state = {}
+    init = [p.detach().clone() for p in pc]
+    for step in range(5):
+        torch.manual_seed(step)
+        x = torch.randn(32, 128)
+        loss_g = model_gpu(x.to(DEV)).pow(2).mean()
+        opt.zero_grad()
+        loss_g.backward()
+        opt.step()
+        loss_c = model(x).pow(2).mean()
+        for p in pc:
+            p.grad = None
+        loss_c.backward()
+        O.muon_reference_step(groups, state, ns=O.ns_fp32)
+    for a, b, p0 in zip(pg, pc, init):
+        a = a.detach().cpu()
+        assert torch.isfinite(a).all()
+        assert O.rel_fro(a - p0, b.detach() - p0) < 0.05
+        assert O.rel_fro(a, b.detach()) < 0.01
+
+
+def test_bf16_params_and_state_dict_roundtrip(cuda_lib):
+    from muon_fused import FusedMuon
+
+    torch.manual_seed(1)
+    p = torch.nn.Parameter(torch.randn(512, 1024, device=DEV, dtype=torch.bfloat16) * 0.02)
+    q = torch.nn.Parameter(p.detach().clone())
+    o1 = FusedMuon([{"params": [p], "use_muon": True}], lr=0.02)
+    o2 = FusedMuon([{"params": [q], "use_muon": True}], lr=0.02)
+    grads = [torch.randn(512, 1024, device=DEV, dtype=torch.bfloat16) * 1e-3 for _ in range(3)]
+    p.grad = grads[0]
+    o1.step()
+    q.grad = grads[0]
+    o2.step()
+    o2b = FusedMuon([{"params": [q], "use_muon": True}], lr=0.02)
+    o2b.load_state_dict(o2.state_dict())
+    for g in grads[1:]:
+        p.grad, q.grad = g, g.clone()
+        o1.step()
+        o2b.step()
+    torch.cuda.synchronize()
+    assert torch.equal(p, q)
+    assert o1.state[p]["momentum_buffer"].dtype == torch.bfloat16
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("nesterov", [True, False])
+def test_fused_elementwise_bit_identical_to_torch_ops(cuda_lib, dtype, nesterov):
+    """fm_muon_momentum / fm_muon_apply reproduce the reference's torch ops
+    (optimizer.py:144-147 and :161-163) bit for bit on the same device."""
+    from muon_fused import _lib
+    from muon_fused.optimizer import FusedMuon
+
+    torch.manual_seed(3)
+    n = 1 << 20 | 77  # ragged length
+    mu, lr, wd = 0.95, 0.02, 0.1
+    buf = torch.randn(n, device=DEV).to(dtype) * 1e-3
+    g = torch.randn(n, device=DEV).to(dtype) * 1e-3
+    ref_buf = buf.clone().mul_(mu).add_(g)
+    ref_dir = (g.add(ref_buf, alpha=mu) if nesterov else ref_buf).to(torch.bfloat16)
+    d = torch.empty(n, dtype=torch.bfloat16, device=DEV)
+    dt = {torch.float32: _lib.FM_DT_F32, torch.bfloat16: _lib.FM_DT_BF16,
+          torch.float16: _lib.FM_DT_F16}[dtype]
+    stream = torch.cuda.current_stream().cuda_stream
+    _lib.check(cuda_lib.fm_muon_momentum(buf.data_ptr(), g.data_ptr(), d.data_ptr(), n, dt, mu,
+                                         int(nesterov), stream), "momentum")
+    torch.cuda.synchronize()
+    assert torch.equal(buf, ref_buf)
+    assert torch.equal(d, ref_dir)
+
+    p = torch.randn(n, device=DEV).to(dtype) * 0.02
+    u = torch.randn(n, device=DEV, dtype=torch.bfloat16) * 0.05
+    alpha = -FusedMuon.adjust_lr_for_muon(lr, (1024, 4096))
+    ref_p = p.clone().mul_(1 - lr * wd).add_(u, alpha=alpha)
+    _lib.check(cuda_lib.fm_muon_apply(p.data_ptr(), dt, u.data_ptr(), n, 1 - lr * wd, alpha,
+                                      stream), "apply")
+    torch.cuda.synchronize()
+    assert torch.equal(p, ref_p)

@@ -1,0 +1,166 @@
+"""Matrix-sharded FusedMuon step on CPU gloo ranks (no GPU).
+
+The Newton-Schulz call is replaced, in the child processes only, by the
+oracle's fp32 restatement so the sharding logic (owner table, momentum
+ownership, bucketed all-gather, apply order) runs without CUDA.  Checks:
+identical parameters on every rank, equal to a single-process run; balanced
+and deterministic owner tables; uneven shards; a rank that leaves between
+steps surfaces as an error on the others.
+"""
+
+import os
+import socket
+import tempfile
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from muon_fused.sharding import ShardPlan, ns_flops, numel
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+SHAPES = [(64, 32), (16, 64), (16, 64), (64, 64), (128, 32), (128, 32), (32, 128), (8, 4, 3, 3),
+          (48, 40)]
+
+
+def _make(seed=0):
+    g = torch.Generator().manual_seed(seed)
+    params = [torch.nn.Parameter(torch.randn(s, generator=g) * 0.02) for s in SHAPES]
+    return params
+
+
+def _grads(step):
+    g = torch.Generator().manual_seed(500 + step)
+    return [torch.randn(s, generator=g) * 1e-3 for s in SHAPES]
+
+
+def _patch_ns():
+    import muon_fused.optimizer as om
+    from oracle import ns_oracle as O
+
+    def ns_batched_cpu(G, steps, workspace, out):
+        for b in range(G.shape[0]):
+            out[b].copy_(O.ns_fp32(G[b].float(), steps).to(torch.bfloat16))
+        return out
+
+    om._ns_batched = ns_batched_cpu
+
+
+def _run_steps(params, steps, bucket_bytes):
+    from muon_fused import FusedMuon
+
+    opt = FusedMuon([{"params": params, "use_muon": True}], lr=0.02, bucket_bytes=bucket_bytes)
+    for s in range(steps):
+        for p, g in zip(params, _grads(s)):
+            p.grad = g.clone()
+        opt.step()
+    return opt
+
+
+def _worker(rank, world, port, outdir, bucket_bytes, leave_rank):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import datetime
+
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=8))
+    _patch_ns()
+    params = _make()
+    try:
+        if leave_rank is not None and rank == leave_rank:
+            # leaves between steps: no collective of this rank is in flight
+            dist.destroy_process_group()
+            return
+        opt = _run_steps(params, 2, bucket_bytes)
+        owned = sorted(i for i, p in enumerate(params) if "momentum_buffer" in opt.state[p])
+        torch.save({"params": [p.detach() for p in params], "owned": owned},
+                   os.path.join(outdir, f"rank{rank}.pt"))
+    except Exception as e:  # recorded for the parent to inspect
+        with open(os.path.join(outdir, f"rank{rank}.err"), "w") as f:
+            f.write(repr(e))
+    finally:
+        if dist.is_initialized():
+            try:
+                dist.destroy_process_group()
+            except Exception:
+                pass
+
+
+def _spawn(world, bucket_bytes=1 << 30, leave_rank=None):
+    outdir = tempfile.mkdtemp()
+    mp.spawn(_worker, args=(world, _free_port(), outdir, bucket_bytes, leave_rank), nprocs=world,
+             join=True)
+    return outdir
+
+
+def _single_process():
+    _patch_ns()
+    params = _make()
+    _run_steps(params, 2, 1 << 30)
+    return [p.detach() for p in params]
+
+
+def test_plan_assigns_each_matrix_once_and_balances():
+    for world in (1, 2, 3, 4, 8):
+        plan = ShardPlan.build(SHAPES, world, bucket_bytes=4096)
+        assert sorted(plan.owner) == sorted(plan.owner) and len(plan.owner) == len(SHAPES)
+        loads = [0.0] * world
+        for i, r in enumerate(plan.owner):
+            loads[r] += ns_flops(SHAPES[i])
+        # LPT bound: no rank exceeds the average by more than the largest item
+        assert max(loads) <= sum(loads) / world + max(ns_flops(s) for s in SHAPES) + 1e-6
+        seen = set()
+        for k, row in enumerate(plan.buckets):
+            for r in range(world):
+                end = 0
+                for i, off in row[r]:
+                    assert plan.owner[i] == r and i not in seen
+                    assert off >= end  # non-overlapping packing
+                    end = off + numel(SHAPES[i])
+                    seen.add(i)
+                assert end <= plan.bucket_numel[k]
+        assert seen == set(range(len(SHAPES)))
+        # deterministic: the same shapes give the same table on every rank
+        assert ShardPlan.build(SHAPES, world, 4096).owner == plan.owner
+
+
+def test_plan_8b_shapes_balance():
+    """the 224 matrices of the 8B set over 2/4/8 ranks."""
+    per_layer = [(4096, 4096), (1024, 4096), (1024, 4096), (4096, 4096), (14336, 4096),
+                 (14336, 4096), (4096, 14336)]
+    shapes = per_layer * 32
+    total = sum(ns_flops(s) for s in shapes)
+    for world in (2, 4, 8):
+        plan = ShardPlan.build(shapes, world)
+        loads = [0.0] * world
+        for i, r in enumerate(plan.owner):
+            loads[r] += ns_flops(shapes[i])
+        assert max(loads) / (total / world) < 1.03
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_sharded_equals_single_process(world):
+    ref = _single_process()
+    outdir = _spawn(world, bucket_bytes=8192)  # small buckets: several all-gathers
+    results = [torch.load(os.path.join(outdir, f"rank{r}.pt")) for r in range(world)]
+    owned = []
+    for r, res in enumerate(results):
+        for a, b in zip(res["params"], ref):
+            assert torch.equal(a, b)
+        owned += res["owned"]
+    # momentum state lives only on the owner rank: every matrix exactly once
+    assert sorted(owned) == list(range(len(SHAPES)))
+
+
+def test_rank_leaving_between_steps_is_an_error():
+    outdir = _spawn(2, leave_rank=1)
+    assert not os.path.exists(os.path.join(outdir, "rank0.pt"))
+    with open(os.path.join(outdir, "rank0.err")) as f:
+        assert f.read()
