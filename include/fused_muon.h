@@ -109,6 +109,17 @@ int fm_ns_step_debug(const void* X, int64_t m, int64_t n, int64_t ldx, void* A, 
 int fm_device_error(uint32_t* code);
 
 /*
+ * Failure-detection self-test: launches one GEMM whose loads are withheld,
+ * so its pipeline wait runs out (after about two seconds) and the kernel
+ * ends, reporting code 1 ("MMA warp timed out waiting for a stage") through
+ * fm_device_error().  The context stays usable.  Nothing on the GPU faults,
+ * traps or hangs.
+ * Replaces: nothing; the reference has no failure detection beyond a silent
+ * Python fallback (muon_fused/ns_step.py:117-120).
+ */
+int fm_selftest_wait_timeout(void* stream);
+
+/*
  * Allocation-free form of fm_fused_newton_schulz, for callers that cannot
  * call cudaMalloc: code running inside a fixed memory budget (a host
  * framework that owns all device memory through its own pool), or code on a

@@ -34,6 +34,7 @@ SIGNATURES = {
     "fm_newton_schulz_step": (_c_int, [_vp, _i64, _i64, _i64, _vp, _vp, _u64, _vp]),
     "fm_ns_step_debug": (_c_int, [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _u64, _vp]),
     "fm_device_error": (_c_int, [ctypes.POINTER(ctypes.c_uint32)]),
+    "fm_selftest_wait_timeout": (_c_int, [_vp]),
     "fm_fused_newton_schulz_noalloc": (_c_int, [_vp, _c_int, _i64, _i64, _i64, _vp, _c_int, _vp]),
     "fm_muon_momentum": (_c_int, [_vp, _vp, _vp, _i64, _c_int, ctypes.c_float, _c_int, _vp]),
     "fm_muon_apply": (_c_int, [_vp, _c_int, _vp, _i64, ctypes.c_float, ctypes.c_float, _vp]),

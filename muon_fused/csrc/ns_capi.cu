@@ -718,6 +718,29 @@ int fm_fused_newton_schulz_noalloc(const void* G, int dtype, int64_t rows, int64
                                 FM_STATIC_SCRATCH_BYTES, stream);
 }
 
+int fm_selftest_wait_timeout(void* stream) {
+  DeviceState* ds;
+  if (int rc = device_state(&ds)) return rc;
+  // One single-CTA GEMM launch over a tiny valid operand whose producer is
+  // told to issue nothing: the MMA warp's wait on the first stage has nothing
+  // to wait for, gives up after its budget, records kErrWaitFull and the CTA
+  // frees its TMEM and exits.  No memory is written; nothing is allocated
+  // beyond a 2 KB scratch operand.
+  static __nv_bfloat16* operand[kMaxDevices] = {};
+  int dev = 0;
+  FM_CUDA(cudaGetDevice(&dev));
+  if (!operand[dev]) FM_CUDA(cudaMalloc(&operand[dev], 128 * 8 * sizeof(__nv_bfloat16)));
+  CUtensorMap map;
+  if (int rc = make_map(&map, operand[dev], 1, 128, 8, 8, 0, kBK, kBM)) return rc;
+  GemmArgs g{};
+  g.M = 128; g.N = 128; g.K = 8;
+  g.num_tiles = 1;
+  g.out = operand[dev]; g.ld_out = 8;
+  g.batch = 1; g.tiles = 1; g.split = 1; g.kb_per_split = 1;
+  g.starve = 1;
+  return launch_gemm<kSyrk>(*ds, map, map, g, static_cast<cudaStream_t>(stream));
+}
+
 int fm_device_error(uint32_t* code) {
   if (!code) return fail(FM_E_INVALID, "code is null");
   DeviceState* ds;

