@@ -566,7 +566,7 @@ int fm_ns_step_debug(const void* X, int64_t m, int64_t n, int64_t ldx, void* A, 
 
 namespace {
 int ew_grid(long long n, const DeviceState& ds) {
-  const long long blocks = (n + kEwThreads - 1) / kEwThreads;
+  const long long blocks = (n / 8 + kEwThreads - 1) / kEwThreads;
   return int(std::max<long long>(1, std::min<long long>(blocks, ds.sm_count * 8ll)));
 }
 }  // namespace

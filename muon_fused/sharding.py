@@ -149,11 +149,20 @@ def run_sharded(plan: ShardPlan, rank: int, pg, device, compute, apply) -> None:
         recv = torch.empty(world * size, dtype=torch.bfloat16, device=device)
         work = _all_gather(recv, send, pg, world)
         pending.append((k, recv, work, send))
-    for k, recv, work, _send in pending:
-        work.wait()
-        size = plan.bucket_numel[k]
-        for r in range(world):
-            base = r * size
-            for i, off in plan.buckets[k][r]:
-                n = numel(plan.shapes[i])
-                apply(i, recv[base + off:base + off + n].view(plan.shapes[i]))
+        # Bucket k-1's gather ran while bucket k was computed; apply it now so
+        # only the last bucket's gather + apply remain after the compute.
+        if len(pending) > 1:
+            _apply_bucket(plan, pending.pop(0), apply)
+    for item in pending:
+        _apply_bucket(plan, item, apply)
+
+
+def _apply_bucket(plan: ShardPlan, item, apply) -> None:
+    k, recv, work, _send = item
+    work.wait()
+    size = plan.bucket_numel[k]
+    for r in range(plan.world):
+        base = r * size
+        for i, off in plan.buckets[k][r]:
+            n = numel(plan.shapes[i])
+            apply(i, recv[base + off:base + off + n].view(plan.shapes[i]))
