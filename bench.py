@@ -298,7 +298,7 @@ def bench_ns(args, peaks, peak_src):
     avg_dom = st[dom][0] / st[dom][1]
     achieved = stage_flops[dom] / (avg_dom * 1e-3) / 1e12
     peak = float(peaks["bf16_tflops"])
-    roofline = {"bound": "tensor", "kernel": "ns_gemm_kernel<kBX> (X' = d*X + Boff*X)",
+    roofline = {"bound": "tensor", "kernel": ("ns_gemm_pair_kernel<kBX>" if min(m, n) > 256 else "ns_gemm_kernel<kBX>") + " (X' = d*X + Boff*X)",
                 "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
                 "frac": round(achieved / peak, 4), "peak_source": f"{peak_src} bf16_tflops (burst)",
                 "traffic": None, "stages": stages}
@@ -399,7 +399,7 @@ def bench_muon(args, world, rank, peaks, peak_src):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--steps", type=int, default=400)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--workload", choices=["ns", "muon1b", "muon8b"], default=None)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
