@@ -44,7 +44,8 @@ constexpr int kTileABytes = kBM * kBK * 2;  // 16 KB
 constexpr int kTileBBytes = kBN * kBK * 2;  // 32 KB
 constexpr int kStageBytes = kTileABytes + kTileBBytes;
 constexpr int kTmemCols = 2 * kBN;  // two fp32 accumulators
-constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align slack*/ + 256 /*barriers*/;
+constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align slack*/ + 256 /*barriers*/ +
+                           4 * 32 * 34 * 2 /*transpose buffers, kTBufBytes*/;
 
 // Newton-Schulz quintic coefficients (reference muon_fused/ns_step.py:39).
 constexpr float kNsA = 3.4445f;
@@ -211,6 +212,35 @@ __device__ __forceinline__ void store_row32(__nv_bfloat16* rowp, int c0, int nco
   }
 }
 
+// Per-warp shared buffer for 32 x 32 transposed stores: rows of 34 bf16
+// (17 words, odd, so the row-wise 4-byte writes hit 32 distinct banks).
+constexpr int kTPitch = 34;
+constexpr int kTBufBytes = 4 * 32 * kTPitch * 2;  // four epilogue warps
+
+// out[(c0 + l) * ld + row0w + j] = v_j[l] for the warp's 32 rows j and the
+// chunk's 32 columns l: the chunk goes through shared memory so that each lane
+// writes one output row of 64 bytes as four 16-byte stores (instead of 32
+// two-byte stores per lane).  All 32 rows and columns must be in bounds and
+// the output rows 16-byte aligned.
+__device__ __forceinline__ void store_transposed32(__nv_bfloat16* out, long long ld, int row0w,
+                                                   int c0, int lane, __nv_bfloat16* tb,
+                                                   const float (&v)[32]) {
+  __syncwarp();  // the previous chunk's reads are done
+  uint32_t* trow = reinterpret_cast<uint32_t*>(tb + lane * kTPitch);
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * k], v[2 * k + 1]);
+    trow[k] = *reinterpret_cast<uint32_t*>(&h);
+  }
+  __syncwarp();
+  __align__(16) __nv_bfloat16 o[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) o[j] = tb[j * kTPitch + lane];
+  uint4* dst = reinterpret_cast<uint4*>(out + static_cast<long long>(c0 + lane) * ld + row0w);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) dst[q] = reinterpret_cast<const uint4*>(o)[q];
+}
+
 // Number of 32-column chunks of a tile row block that warp rows row0w.. store:
 // a prefix (columns below N; for the SYRK modes also at or left of the warp's
 // last row).
@@ -264,6 +294,7 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& g, uint32_t tmem_a
                                               int row0w, int col0, int lane, bool out_vec,
                                               bool aux_vec, uint64_t* accf_bar, uint32_t acc_phase,
                                               volatile int* abort_flag,
+                                              __nv_bfloat16* tbuf,
                                               const float* parts = nullptr, int split = 1) {
   const int row = row0w + lane;
   const bool row_ok = row < g.M;
@@ -300,11 +331,11 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& g, uint32_t tmem_a
     } else {
       tmem_ld_32x32b_x32(tmem_acc + c * 32 + (static_cast<uint32_t>(q * 32) << 16), v);
     }
-    if (row_ok) {
-      if constexpr (MODE == kSyrk) {
-        store_row32(g.out + row * g.ld_out, c0, g.N, row, true, out_vec, v);
-        store_mirror32(g.out, g.ld_out, c0, g.N, row, v);
-      } else if constexpr (MODE == kPoly) {
+    // All 32 rows and columns of this chunk in bounds (warp-uniform): the
+    // column-wise stores (mirror, transposed output) can go through smem.
+    const bool whole = row0w + 31 < g.M && c0 + 31 < g.N && out_vec;
+    if constexpr (MODE == kPoly) {
+      if (row_ok) {
         float av[32];
 #pragma unroll
         for (int k = 0; k < 4; ++k) unpack8_bf16(araw[k], av + 8 * k);
@@ -317,24 +348,34 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& g, uint32_t tmem_a
           }
           v[k] = x;
         }
-        store_row32(g.out + row * g.ld_out, c0, g.N, row, true, out_vec, v);
+      }
+    }
+    if constexpr (MODE != kBX) {
+      if (row_ok) store_row32(g.out + row * g.ld_out, c0, g.N, row, true, out_vec, v);
+      if (whole && c0 + 31 < row0w) {  // chunk strictly below the diagonal
+        store_transposed32(g.out, g.ld_out, row0w, c0, lane, tbuf, v);
+      } else if (row_ok) {
         store_mirror32(g.out, g.ld_out, c0, g.N, row, v);
-      } else {  // kBX
-        float xv[32];
+      }
+    } else {
+      float xv[32];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) unpack8_bf16(araw[k], xv + 8 * k);
+      for (int k = 0; k < 4; ++k) unpack8_bf16(araw[k], xv + 8 * k);
 #pragma unroll
-        for (int k = 0; k < 32; ++k) v[k] = fmaf(dval, xv[k], v[k]);
-        if (g.transpose_out) {
+      for (int k = 0; k < 32; ++k) v[k] = fmaf(dval, xv[k], v[k]);
+      if (g.transpose_out) {
+        if (whole) {
+          store_transposed32(g.out, g.ld_out, row0w, c0, lane, tbuf, v);
+        } else if (row_ok) {
 #pragma unroll
           for (int k = 0; k < 32; ++k) {
             const int col = c0 + k;
             if (col < g.N)
               g.out[static_cast<long long>(col) * g.ld_out + row] = __float2bfloat16_rn(v[k]);
           }
-        } else {
-          store_row32(g.out + row * g.ld_out, c0, g.N, row, false, out_vec, v);
         }
+      } else if (row_ok) {
+        store_row32(g.out + row * g.ld_out, c0, g.N, row, false, out_vec, v);
       }
     }
     if constexpr (MODE != kSyrk) {
@@ -362,6 +403,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* accf_bar = empty_bar + kStages;  // accumulator ready  [2]
   uint64_t* acce_bar = accf_bar + 2;         // accumulator drained [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce_bar + 2);
+  // per-warp transpose buffers of the epilogue, after the 256-byte barrier block
+  __nv_bfloat16* tbuf = reinterpret_cast<__nv_bfloat16*>(smem + kStages * kStageBytes + 256);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -491,7 +534,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       int ti, tj;
       tile_coords<MODE>(g, t, ti, tj);
       if (!epilogue_tile<MODE>(g, tmem_base + acc * kBN, q, ti * kBM + q * 32, tj * kBN, lane,
-                               out_vec, aux_vec, &accf_bar[acc], acc_phase, abort_flag))
+                               out_vec, aux_vec, &accf_bar[acc], acc_phase, abort_flag,
+                               tbuf + (warp - 2) * 32 * kTPitch))
         break;
       if (lane == 0) mbar_arrive(&acce_bar[acc]);
       if (++acc == 2) {
