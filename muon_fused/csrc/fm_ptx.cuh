@@ -87,6 +87,18 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// ------------------------------------------------ programmatic dependent launch
+// Kernels are launched with programmatic stream serialization: a kernel may
+// start (and run its prologue) while the previous one drains.  pdl_wait()
+// blocks until the previous grid has completed and its memory is visible, so
+// every thread calls it before its first global-memory access; pdl_trigger()
+// lets the next grid launch once every CTA of this one has called it or exited.
+// Without the launch attribute both are no-ops.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");

@@ -270,6 +270,33 @@ Workspace layout(long long batch, long long m, long long n, void* base) {
   return w;
 }
 
+// Launch with programmatic stream serialization (PDL): the kernel may begin
+// while the previous kernel on the stream drains; it waits (griddepcontrol)
+// before touching global memory.  cluster2 adds a 2-CTA cluster dimension.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t st, bool cluster2, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  int n = 1;
+  if (cluster2) {
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 2;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    n = 2;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 template <int MODE>
 int launch_gemm(const DeviceState& ds, const CUtensorMap& ma, const CUtensorMap& mb, GemmArgs g,
                 cudaStream_t st) {
@@ -277,8 +304,8 @@ int launch_gemm(const DeviceState& ds, const CUtensorMap& ma, const CUtensorMap&
   if (g.num_tiles <= 0) return FM_OK;
   const int grid = std::min(g.num_tiles, ds.sm_count);
   const long long tm = timer_begin(MODE, st);
-  ns_gemm_kernel<MODE><<<grid, kThreads, kSmemBytes, st>>>(ma, mb, g);
-  FM_CUDA(cudaGetLastError());
+  FM_CUDA(launch_pdl(ns_gemm_kernel<MODE>, dim3(grid), dim3(kThreads), kSmemBytes, st, false, ma,
+                     mb, g));
   timer_end(tm, st);
   return FM_OK;
 }
@@ -291,20 +318,9 @@ int launch_gemm_pair(const DeviceState& ds, const CUtensorMap& ma, const CUtenso
   g.err = ds.err_word;
   if (g.num_tiles <= 0) return FM_OK;
   const int pairs = std::min(g.num_tiles, ds.sm_count / 2);
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(2 * pairs);
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = kPairSmemBytes;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
   const long long tm = timer_begin(MODE, st);
-  FM_CUDA(cudaLaunchKernelEx(&cfg, ns_gemm_pair_kernel<MODE>, ma, mb, g));
+  FM_CUDA(launch_pdl(ns_gemm_pair_kernel<MODE>, dim3(2 * pairs), dim3(kThreads), kPairSmemBytes, st,
+                     true, ma, mb, g));
   timer_end(tm, st);
   return FM_OK;
 }
@@ -427,23 +443,26 @@ int ns_run(const void* G, int dtype, long long batch, long long rows, long long 
   const long long tm = timer_begin(3, st);
   if (P.split_slots > 0) FM_CUDA(cudaMemsetAsync(w.counters, 0, w.counter_bytes, st));
   const long long bs_g_eff = batch > 1 ? bs_g : 0;
-  sumsq_kernel<<<dim3(pg, unsigned(batch)), kPrepThreads, 0, st>>>(
-      G, dtype, rows, cols, ldg, bs_g_eff, w.partials);
+  FM_CUDA(launch_pdl(sumsq_kernel, dim3(pg, unsigned(batch)), dim3(kPrepThreads), 0, st, false,
+                     G, dtype, rows, cols, ldg, bs_g_eff, w.partials));
   FM_CUDA(cudaGetLastError());
   if (steps == 0) {  // normalised input, original orientation
-    scale_kernel<<<dim3(pg, unsigned(batch)), kPrepThreads, 0, st>>>(
-        G, dtype, rows, cols, ldg, bs_g_eff, w.partials, pg, o, cols, bs_out);
+    FM_CUDA(launch_pdl(scale_kernel, dim3(pg, unsigned(batch)), dim3(kPrepThreads), 0, st, false,
+                       G, dtype, rows, cols, ldg, bs_g_eff, (const float*)w.partials, pg, o,
+                       (long long)cols, bs_out));
     FM_CUDA(cudaGetLastError());
     timer_end(tm, st);
     return FM_OK;
   }
   if (tall) {
     dim3 grid(unsigned((cols + kTT - 1) / kTT), unsigned((rows + kTT - 1) / kTT), unsigned(batch));
-    scale_transpose_kernel<<<grid, kPrepThreads, 0, st>>>(G, dtype, rows, cols, ldg, bs_g_eff,
-                                                          w.partials, pg, w.X[0], w.ldx, w.xs);
+    FM_CUDA(launch_pdl(scale_transpose_kernel, grid, dim3(kPrepThreads), 0, st, false, G, dtype,
+                       rows, cols, ldg, bs_g_eff, (const float*)w.partials, pg, w.X[0], w.ldx,
+                       w.xs));
   } else {
-    scale_kernel<<<dim3(pg, unsigned(batch)), kPrepThreads, 0, st>>>(
-        G, dtype, rows, cols, ldg, bs_g_eff, w.partials, pg, w.X[0], w.ldx, w.xs);
+    FM_CUDA(launch_pdl(scale_kernel, dim3(pg, unsigned(batch)), dim3(kPrepThreads), 0, st, false,
+                       G, dtype, rows, cols, ldg, bs_g_eff, (const float*)w.partials, pg, w.X[0],
+                       w.ldx, w.xs));
   }
   FM_CUDA(cudaGetLastError());
   timer_end(tm, st);
@@ -755,3 +774,12 @@ int fm_device_error(uint32_t* code) {
 }
 
 }  // extern "C"
+
+#ifdef FM_TRACE
+// Development only: copy the CTA-pair timeline (128 x 40 u64) to host memory.
+extern "C" int fm_trace_read(void* host) {
+  FM_CUDA(cudaDeviceSynchronize());
+  FM_CUDA(cudaMemcpyFromSymbol(host, fm::g_fm_trace, sizeof(fm::g_fm_trace)));
+  return FM_OK;
+}
+#endif

@@ -68,6 +68,26 @@ __device__ __forceinline__ PairUnit pair_unit(const GemmArgs& g, int u, int num_
   return w;
 }
 
+#ifdef FM_TRACE
+// Development timeline (built only with -DFM_TRACE): per GEMM mode and pair,
+// slot 0 = start of work, then per unit k: 1+3k MMA start, 2+3k MMAs issued,
+// 3+3k epilogue done (leader CTA); slot 38 = kernel entry, 39 = kernel exit.
+// Read with fm_trace_read.
+__device__ unsigned long long g_fm_trace[3][128][40];
+#define FM_TRACE_MARK(slot)                                                       \
+  do {                                                                            \
+    if ((slot) < 38) g_fm_trace[MODE][pair][(slot)] = globaltimer();              \
+  } while (0)
+#define FM_TRACE_EDGE(slot) g_fm_trace[MODE][pair][(slot)] = globaltimer()
+#else
+#define FM_TRACE_MARK(slot) \
+  do {                      \
+  } while (0)
+#define FM_TRACE_EDGE(slot) \
+  do {                      \
+  } while (0)
+#endif
+
 template <int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
     ns_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA,
@@ -92,6 +112,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int pair = blockIdx.x >> 1;
   const int num_pairs = gridDim.x >> 1;
   const int num_kb = (g.K + kBK - 1) / kBK;
+  if (threadIdx.x == 0 && rank == 0) FM_TRACE_EDGE(38);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kPairStages; ++s) {
@@ -115,6 +136,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   cluster_sync();  // barriers of both CTAs initialised before any remote use
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();  // the previous kernel's outputs are complete from here on
+  if (threadIdx.x == 0 && rank == 0) FM_TRACE_MARK(0);
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer (both CTAs)
@@ -150,6 +173,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
+    if (lane == 0) pdl_trigger();  // all loads issued: the next kernel may launch
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer (leader)
     if (rank == 0 && lane == 0) {
@@ -157,6 +181,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
+      int nunit = 0;  // trace index only
       uint32_t acc_phase = 0;
       bool ok = true;
       for (int t = pair; t < g.num_tiles && ok; t += num_pairs) {
@@ -168,6 +193,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const PairUnit w = pair_unit<MODE>(g, t, num_kb);
         const uint32_t d_tmem = tmem_base + acc * kPairBN;
+        FM_TRACE_MARK(1 + 3 * nunit);
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait_cluster(&full_bar[stage], phase, abort_flag, g.err, kErrWaitFull)) {
             ok = false;
@@ -195,6 +221,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (!ok) break;
         tc_commit_pair(&accf_bar[acc], 0x3);  // accumulator complete in both CTAs
+        FM_TRACE_MARK(2 + 3 * nunit);
+        ++nunit;
         if (++acc == 2) {
           acc = 0;
           acc_phase ^= 1;
@@ -208,6 +236,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool aux_vec = ((reinterpret_cast<uintptr_t>(g.aux) | (g.ld_aux * 2)) & 15) == 0;
     volatile int* last_flag = abort_flag + 1;  // smem word shared by the epilogue warps
     int acc = 0;
+    int nunit = 0;  // trace index only
     uint32_t acc_phase = 0;
     for (int t = pair; t < g.num_tiles; t += num_pairs) {
       const PairUnit w = pair_unit<MODE>(g, t, num_kb);
@@ -221,6 +250,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                                  acc_phase, abort_flag, tbuf + (warp - 2) * 32 * kTPitch))
           break;
         if (lane == 0) mbar_arrive_remote(acce_remote);
+        if (lane == 0 && q == 2 && rank == 0) FM_TRACE_MARK(3 + 3 * nunit);
+        ++nunit;
       } else {
         // this (matrix, tile, CTA half)'s partial slots, split 0 first
         const long long slot = (static_cast<long long>(w.b) * g.tiles + w.tile) * 2 + rank;
@@ -268,6 +299,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc_pair(tmem_base, kTmemCols);
   }
+  if (threadIdx.x == 0 && rank == 0) FM_TRACE_EDGE(39);
 }
 
 }  // namespace fm

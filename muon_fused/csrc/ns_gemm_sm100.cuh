@@ -433,6 +433,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();  // the previous kernel's outputs are complete from here on
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -470,6 +471,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
+    if (lane == 0) pdl_trigger();  // all loads issued: the next kernel may launch
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {

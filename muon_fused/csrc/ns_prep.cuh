@@ -17,6 +17,8 @@
 #include <cuda_fp16.h>
 #include <cstdint>
 
+#include "fm_ptx.cuh"
+
 namespace fm {
 
 // Input element codes of the C ABI (FM_DT_* in include/fused_muon.h).
@@ -106,6 +108,7 @@ __global__ void __launch_bounds__(kPrepThreads) sumsq_kernel(const void* __restr
                                                              long long rows, long long cols,
                                                              long long ldg, long long bs_g,
                                                              float* partials) {
+  pdl_wait();
   const void* G = batch_ptr(G0, dtype, bs_g, blockIdx.y);
   partials += static_cast<long long>(blockIdx.y) * kMaxPartials;
   const ChunkGrid g{rows, cols, ldg, (cols + 7) / 8};
@@ -141,6 +144,7 @@ __global__ void __launch_bounds__(kPrepThreads) sumsq_kernel(const void* __restr
     v = warp_sum(v);
     if (threadIdx.x == 0) partials[blockIdx.x] = v;
   }
+  pdl_trigger();
 }
 
 // Denominator ||G||_F + 1e-7, reduced from the partials in a fixed order.
@@ -164,6 +168,7 @@ __global__ void __launch_bounds__(kPrepThreads) scale_kernel(const void* __restr
                                                              const float* partials, int nparts,
                                                              __nv_bfloat16* X, long long ldx,
                                                              long long xs) {
+  pdl_wait();
   const void* G = batch_ptr(G0, dtype, bs_g, blockIdx.y);
   if (partials) partials += static_cast<long long>(blockIdx.y) * kMaxPartials;
   X += static_cast<long long>(blockIdx.y) * xs;
@@ -199,6 +204,7 @@ __global__ void __launch_bounds__(kPrepThreads) scale_kernel(const void* __restr
       }
     }
   }
+  pdl_trigger();
 }
 
 // Transposing variant for tall G (rows > cols): X[c][r] = bf16(bf16(G[r][c]) / den).
@@ -208,6 +214,7 @@ __global__ void __launch_bounds__(kPrepThreads) scale_transpose_kernel(
     const void* __restrict__ G0, int dtype, long long rows, long long cols, long long ldg,
     long long bs_g, const float* partials, int nparts, __nv_bfloat16* X, long long ldx,
     long long xs) {
+  pdl_wait();
   const void* G = batch_ptr(G0, dtype, bs_g, blockIdx.z);
   partials += static_cast<long long>(blockIdx.z) * kMaxPartials;
   X += static_cast<long long>(blockIdx.z) * xs;
@@ -250,6 +257,7 @@ __global__ void __launch_bounds__(kPrepThreads) scale_transpose_kernel(
       for (int k = 0; k < 8 && r + k < rows; ++k) dst[k] = tile[oc * 8 + k][orow];
     }
   }
+  pdl_trigger();
 }
 
 }  // namespace fm
