@@ -245,7 +245,8 @@ def config_for(wl: str, world: int, shape=SHAPE_NS):
     return {"workload": f"fusedmuon_step_{wl}", "matrices": len(shapes), "ns_steps": NS_STEPS,
             "lr": 0.02, "momentum": 0.95, "nesterov": True,
             "l2": "working set (params+grads+momentum) far above L2",
-            "parallelism": f"matrix-sharded dp{world}" if world > 1 else "single"}
+            "parallelism": f"matrix-sharded dp{world}" if world > 1 else "single",
+            "exchange": "n/a"}
 
 
 # --------------------------------------------------------------------------- our arm
@@ -368,7 +369,7 @@ def bench_muon(args, world, rank, peaks, peak_src):
                              device=dev, dtype=torch.bfloat16) * 1e-3
         params.append(p)
     opt = FusedMuon([{"params": params, "use_muon": True}], lr=0.02, momentum=0.95, nesterov=True,
-                    ns_steps=NS_STEPS)
+                    ns_steps=NS_STEPS, collective=args.collective)
     for _ in range(args.warmup):
         opt.step()
     torch.cuda.synchronize()
@@ -403,6 +404,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--workload", choices=["ns", "muon1b", "muon8b"], default=None)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--collective", choices=["nccl", "peer"], default="nccl",
+                    help="sharded-step exchange: NCCL all-gather + apply, or the fused "
+                         "peer-memory gather + apply kernel")
     ap.add_argument("--shape", type=int, nargs=2, default=list(SHAPE_NS),
                     help="ns workload matrix shape (default: the headline 4096 4096)")
     ap.add_argument("--quick", action="store_true",
@@ -441,7 +445,9 @@ def main():
             "ms_per_step": round(r["ms"], 4), "higher_is_better": True,
             "scaling": "weak" if args.workload == "ns" else "strong",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": config_for(args.workload, world, getattr(args, "shape", SHAPE_NS)),
+            "config": dict(config_for(args.workload, world, getattr(args, "shape", SHAPE_NS)),
+                           **({"exchange": args.collective}
+                              if world > 1 and args.workload != "ns" else {})),
             "clocks": r["clocks"], "gpu_launches": r["launches"],
         }
         if r["e2e"] is not None:

@@ -23,6 +23,7 @@
 #include "ns_gemm_sm100.cuh"
 #include "muon_elementwise.cuh"
 #include "ns_prep.cuh"
+#include "peer_apply.cuh"
 
 namespace fm {
 
@@ -130,6 +131,11 @@ int device_state(DeviceState** out) {
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, kPairSmemBytes));
       FM_CUDA(cudaFuncSetAttribute(ns_gemm_pair_kernel<kBX>,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, kPairSmemBytes));
+      // The peer apply kernel runs beside the GEMMs on a side stream: with the
+      // default (small) shared-memory carveout an SM hosting it could not take
+      // a GEMM CTA until it drained, so it asks for the GEMMs' configuration.
+      FM_CUDA(cudaFuncSetAttribute(peer_gather_apply_kernel,
+                                   cudaFuncAttributePreferredSharedMemoryCarveout, 100));
       FM_CUDA(cudaGetSymbolAddress(reinterpret_cast<void**>(&s.err_word), g_device_error));
       if (!g_encode) {
         cudaDriverEntryPointQueryResult q;
@@ -647,6 +653,61 @@ int fm_muon_apply(void* param, int dtype, const void* update, int64_t n, float d
     default:
       return fail(FM_E_INVALID, "fm_muon_apply: unsupported dtype %d", dtype);
   }
+  FM_CUDA(cudaGetLastError());
+  return FM_OK;
+}
+
+int fm_peer_alloc(uint64_t bytes, void** ptr, void* ipc_handle) {
+  if (!ptr || !ipc_handle || bytes == 0) return fail(FM_E_INVALID, "bad fm_peer_alloc arguments");
+  void* p = nullptr;
+  FM_CUDA(cudaMalloc(&p, bytes));
+  cudaError_t e = cudaMemset(p, 0, bytes);
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(ipc_handle), p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return fail(FM_E_CUDA, "fm_peer_alloc: %s", cudaGetErrorString(e));
+  }
+  *ptr = p;
+  return FM_OK;
+}
+
+int fm_peer_open(const void* ipc_handle, void** ptr) {
+  if (!ptr || !ipc_handle) return fail(FM_E_INVALID, "null pointer argument");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, ipc_handle, sizeof(h));
+  FM_CUDA(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess));
+  return FM_OK;
+}
+
+int fm_peer_close(void* ptr) {
+  FM_CUDA(cudaIpcCloseMemHandle(ptr));
+  return FM_OK;
+}
+
+int fm_peer_free(void* ptr) {
+  FM_CUDA(cudaFree(ptr));
+  return FM_OK;
+}
+
+int fm_peer_signal(int64_t* flag, int64_t value, void* stream) {
+  if (!flag) return fail(FM_E_INVALID, "null flag");
+  peer_signal_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(
+      reinterpret_cast<long long*>(flag), static_cast<long long>(value));
+  FM_CUDA(cudaGetLastError());
+  return FM_OK;
+}
+
+int fm_peer_gather_apply(const fm_apply_entry* entries, int nentries, const void* const* peer_src,
+                         int64_t src_shift, const int64_t* const* peer_flags, int flag_index,
+                         int64_t expected, void* stream) {
+  if (nentries <= 0) return FM_OK;
+  if (!entries || !peer_src || !peer_flags) return fail(FM_E_INVALID, "null pointer argument");
+  DeviceState* ds;
+  if (int rc = device_state(&ds)) return rc;
+  peer_gather_apply_kernel<<<ds->sm_count, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      entries, nentries, reinterpret_cast<const __nv_bfloat16* const*>(peer_src), src_shift,
+      reinterpret_cast<const long long* const*>(peer_flags), flag_index,
+      static_cast<long long>(expected), ds->err_word);
   FM_CUDA(cudaGetLastError());
   return FM_OK;
 }

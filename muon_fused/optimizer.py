@@ -63,6 +63,10 @@ class FusedMuon(Optimizer):
         batch_bytes: device memory one batched Newton-Schulz call may use for
             its inputs, outputs and workspace (default 4 GiB); same-shape
             matrices are batched up to this budget.
+        collective: how a sharded step shares the updates: ``"nccl"`` (bucketed
+            NCCL all-gather, then a local apply) or ``"peer"`` (a fused kernel
+            reads each owner's send buffer over NVLink via CUDA IPC and
+            applies the update in the same pass).
     """
 
     def __init__(
@@ -78,6 +82,7 @@ class FusedMuon(Optimizer):
         process_group=None,
         bucket_bytes: int = 256 << 20,
         batch_bytes: int = 4 << 30,
+        collective: str = "nccl",
     ):
         defaults: dict[str, Any] = dict(
             lr=lr, wd=wd, momentum=momentum, nesterov=nesterov, ns_steps=ns_steps,
@@ -90,6 +95,10 @@ class FusedMuon(Optimizer):
         self._batch_bytes = int(batch_bytes)
         self._plans: dict[tuple, Any] = {}
         self._arena: dict[torch.device, torch.Tensor] = {}
+        if collective not in ("nccl", "peer"):
+            raise ValueError(f"collective must be 'nccl' or 'peer', got {collective!r}")
+        self._collective = collective
+        self._exchanges: dict[tuple, Any] = {}
 
     # ------------------------------------------------------------------ helpers
     @staticmethod
@@ -244,7 +253,28 @@ class FusedMuon(Optimizer):
         def apply(i: int, u: torch.Tensor) -> None:
             self._apply_update(params[i], u, group["lr"], group["wd"])
 
-        sharding.run_sharded(plan, rank, pg, params[0].device, compute, apply)
+        dev = params[0].device
+        if self._collective == "peer" and self._peer_ok(params, pg):
+            ex = self._exchanges.get(key)
+            if ex is None:
+                ex = sharding.PeerExchange(plan, rank, pg, dev)
+                self._exchanges[key] = ex
+            lr, wd = group["lr"], group["wd"]
+            decay_alpha = [(float(1 - lr * wd), float(-self.adjust_lr_for_muon(lr, p.shape)))
+                           for p in params]
+            sharding.run_sharded_peer(ex, params, decay_alpha, compute)
+            return
+        sharding.run_sharded(plan, rank, pg, dev, compute, apply)
+
+    @staticmethod
+    def _peer_ok(params, pg) -> bool:
+        """The peer-memory exchange needs NCCL-backed CUDA ranks and contiguous
+        parameters of a dtype the fused update handles."""
+        import torch.distributed as dist
+
+        if dist.get_backend(pg) != "nccl":
+            return False
+        return all(p.is_cuda and p.data.is_contiguous() and p.dtype in _EW_DTYPES for p in params)
 
     # ------------------------------------------------------------------ AdamW
     def _adamw_group(self, group) -> None:

@@ -32,10 +32,11 @@ def _grads(step, device):
     return [(torch.randn(s, generator=g) * 1e-3).to(device) for s in SHAPES]
 
 
-def _run(params, device, steps=2):
+def _run(params, device, steps=3, collective="nccl"):
     from muon_fused import FusedMuon
 
-    opt = FusedMuon([{"params": params, "use_muon": True}], lr=0.02, bucket_bytes=1 << 20)
+    opt = FusedMuon([{"params": params, "use_muon": True}], lr=0.02, bucket_bytes=1 << 20,
+                    collective=collective)
     for s in range(steps):
         for p, g in zip(params, _grads(s, device)):
             p.grad = g
@@ -44,7 +45,7 @@ def _run(params, device, steps=2):
     return [p.detach().cpu() for p in params]
 
 
-def _worker(rank, world, port, outdir):
+def _worker(rank, world, port, outdir, collective):
     import datetime
 
     import torch.distributed as dist
@@ -55,25 +56,38 @@ def _worker(rank, world, port, outdir):
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
                             timeout=datetime.timedelta(seconds=60))
     try:
-        res = _run(_params(dev), dev)
-        torch.save(res, os.path.join(outdir, f"rank{rank}.pt"))
+        res = _run(_params(dev), dev, collective=collective)
+        from muon_fused import _lib
+
+        code = _lib.device_error()
+        assert code == 0, f"rank {rank} ({collective}): device error code {code}"
+        torch.save(res, os.path.join(outdir, f"{collective}{rank}.pt"))
     finally:
         dist.destroy_process_group()
 
 
 def test_sharded_nccl_matches_single_gpu(cuda_lib):
+    """Both exchanges (NCCL all-gather; fused peer-memory gather + apply over
+    NVLink) give every rank the same parameters, bit-identical between the
+    two exchanges, and equal to the single-GPU run up to summation order.
+    Three steps exercise both parities of the peer send buffers."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     ref = _run(_params(torch.device("cuda", 0)), torch.device("cuda", 0))
     outdir = tempfile.mkdtemp()
-    mp.spawn(_worker, args=(2, _port(), outdir), nprocs=2, join=True)
+    for collective in ("nccl", "peer"):
+        mp.spawn(_worker, args=(2, _port(), outdir, collective), nprocs=2, join=True)
     from oracle import ns_oracle as O
 
     init = [p.detach().cpu() for p in _params("cpu")]
-    got = [torch.load(os.path.join(outdir, f"rank{r}.pt")) for r in range(2)]
-    for a, b in zip(got[0], got[1]):
-        assert torch.equal(a, b)  # every rank applied the same gathered updates
+    got = {c: [torch.load(os.path.join(outdir, f"{c}{r}.pt")) for r in range(2)]
+           for c in ("nccl", "peer")}
+    for c in got:
+        for a, b in zip(got[c][0], got[c][1]):
+            assert torch.equal(a, b)  # every rank applied the same updates
+    for a, b in zip(got["nccl"][0], got["peer"][0]):
+        assert torch.equal(a, b)  # same arithmetic, different transport
     # Batches differ between the sharded and the single-GPU run (so may the
     # K-splits): equal up to fp32 summation order inside the GEMMs.
-    for a, b, p0 in zip(got[0], ref, init):
+    for a, b, p0 in zip(got["nccl"][0], ref, init):
         assert O.rel_fro(a - p0, b - p0) <= 5e-3
