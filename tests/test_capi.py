@@ -1,12 +1,10 @@
 """The C-ABI library builds, loads and exports every symbol include/fused_muon.h
 declares; argument validation that happens before any device work."""
 
-import ctypes
 import os
 import re
 
 import pytest
-import torch
 
 from muon_fused import _lib
 from tests.conftest import ROOT
