@@ -207,18 +207,24 @@ def run_reference_arm(args, world, rank):
         fn = lambda: [O.ns_reference_bf16(g, NS_STEPS) for g in gs]
     for _ in range(args.warmup):
         fn()
+    # bounded sample: stop timing after ~60 s of CPU work (at least one step)
     times = []
+    t_start = time.perf_counter()
     for _ in range(args.steps):
         t0 = time.perf_counter()
         fn()
         times.append(time.perf_counter() - t0)
+        if time.perf_counter() - t_start > 60.0:
+            break
     t = statistics.mean(times)
     value = unit_flops / t / 1e12
     line = {
         "impl": "reference", "metric": metric_name(wl), "value": round(value, 4),
-        "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "unit": "TFLOP/s", "n_gpus": world, "steps": len(times), "warmup": args.warmup,
+        "steps_requested": args.steps,
         "ms_per_step": round(t * 1e3, 3), "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "scaling": "weak" if wl == "ns" else "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic",
         "config": config_for(wl, world),
         "cpu_baseline": {"value": round(value, 4), "unit": "TFLOP/s", "cores": threads,
                          "kind": "port", "sample": sample},
