@@ -144,6 +144,46 @@ def flush_l2(buf: torch.Tensor) -> None:
     buf.fill_(1)
 
 
+def pipelined_ns_e2e(G_host, G_dev, out_host, ws, flush, steps, ns) -> float:
+    """ms per step of `steps` NS calls whose inputs come from pinned host memory
+    and whose results go back to it, with copies overlapping the computation
+    (two device input buffers, two host result buffers, one copy stream per
+    direction).  One CUDA-event pair on the compute stream brackets the whole
+    run; every copy is ordered inside it."""
+    stream = torch.cuda.current_stream()
+    up, down = torch.cuda.Stream(), torch.cuda.Stream()
+    uploaded = [torch.cuda.Event() for _ in range(2)]
+    computed = [torch.cuda.Event() for _ in range(2)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    start.record(stream)
+    up.wait_stream(stream)
+    down.wait_stream(stream)
+    with torch.cuda.stream(up):
+        G_dev[0].copy_(G_host, non_blocking=True)
+        uploaded[0].record(up)
+    for i in range(steps):
+        b = i & 1
+        stream.wait_event(uploaded[b])
+        flush_l2(flush)
+        out = ns(G_dev[b], NS_STEPS, ws)
+        computed[b].record(stream)
+        if i + 1 < steps:
+            with torch.cuda.stream(up):
+                if i >= 1:
+                    up.wait_event(computed[b ^ 1])  # step i-1 has read that buffer
+                G_dev[b ^ 1].copy_(G_host, non_blocking=True)
+                uploaded[b ^ 1].record(up)
+        down.wait_event(computed[b])
+        with torch.cuda.stream(down):
+            out_host[b].copy_(out, non_blocking=True)
+        out.record_stream(down)
+    stream.wait_stream(down)
+    end.record(stream)
+    torch.cuda.synchronize()
+    return start.elapsed_time(end) / steps
+
+
 def torch_eager_ns(G: torch.Tensor, steps: int) -> torch.Tensor:
     """The reference's pure-PyTorch NS (muon_fused/ns_step.py:25-55) on the GPU:
     the path a reference user gets on B200, where its sm_80 extension is not
@@ -271,6 +311,7 @@ def bench_ns(args, peaks, peak_src):
 
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(args.steps)]
+    n_launch0 = _lib.launch_count()
     with ClockSampler(torch.cuda.current_device()) as clk:
         for s, e in evs:
             flush_l2(flush)
@@ -278,6 +319,7 @@ def bench_ns(args, peaks, peak_src):
             fused_newton_schulz(G, NS_STEPS, ws)
             e.record(stream)
         torch.cuda.synchronize()
+    launches = _lib.launch_count() - n_launch0
     t_ms = [s.elapsed_time(e) for s, e in evs]
     ms = statistics.mean(t_ms)
     flops = ns_flops(m, n)
@@ -314,27 +356,33 @@ def bench_ns(args, peaks, peak_src):
                                                 + 2.0 * m * m * n) / (ms * 1e-3) / 1e12, 1)}
     if args.quick:
         return {"ms": ms, "flops": flops, "t_ms": t_ms, "roofline": roofline,
-                "clocks": clk.summary(), "e2e": None, "launches": args.steps * (2 + 3 * NS_STEPS),
+                "clocks": clk.summary(), "e2e": None, "launches": launches,
                 "extra": extra}
 
-    # end to end: pinned host G -> device -> NS -> pinned host result
+    # end to end: pinned host G -> device -> NS -> pinned host result.
+    # Serial: each step's copies and NS back to back on one stream.
     G_host = G.cpu().pin_memory()
-    out_host = torch.empty((m, n), dtype=torch.bfloat16).pin_memory()
-    G_dev = torch.empty_like(G)
+    out_host = [torch.empty((m, n), dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    G_dev = [torch.empty_like(G) for _ in range(2)]
     for _ in range(2):
-        G_dev.copy_(G_host, non_blocking=True)
-        out_host.copy_(fused_newton_schulz(G_dev, NS_STEPS, ws), non_blocking=True)
+        G_dev[0].copy_(G_host, non_blocking=True)
+        out_host[0].copy_(fused_newton_schulz(G_dev[0], NS_STEPS, ws), non_blocking=True)
     torch.cuda.synchronize()
     evs2 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
             for _ in range(args.steps)]
     for s, e in evs2:
         flush_l2(flush)
         s.record(stream)
-        G_dev.copy_(G_host, non_blocking=True)
-        out_host.copy_(fused_newton_schulz(G_dev, NS_STEPS, ws), non_blocking=True)
+        G_dev[0].copy_(G_host, non_blocking=True)
+        out_host[0].copy_(fused_newton_schulz(G_dev[0], NS_STEPS, ws), non_blocking=True)
         e.record(stream)
     torch.cuda.synchronize()
-    e2e_ms = statistics.mean(s.elapsed_time(e) for s, e in evs2)
+    serial_ms = statistics.mean(s.elapsed_time(e) for s, e in evs2)
+    # Pipelined (the headline e2e): step i+1's input upload and step i-1's
+    # result download run on two copy streams while step i computes;
+    # double-buffered device inputs, every byte still crosses the link in the
+    # timed region.
+    e2e_ms = pipelined_ns_e2e(G_host, G_dev, out_host, ws, flush, args.steps, fused_newton_schulz)
 
     # the reference's PyTorch path on this GPU (what a reference user runs on B200)
     for _ in range(3):
@@ -354,8 +402,12 @@ def bench_ns(args, peaks, peak_src):
         "ms": ms, "flops": flops, "t_ms": t_ms, "roofline": roofline, "clocks": clk.summary(),
         "e2e": {"value": round(flops / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
                 "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": G_host.nbytes,
-                "d2h_bytes_per_step": out_host.nbytes},
-        "launches": args.steps * (2 + 3 * NS_STEPS),
+                "d2h_bytes_per_step": out_host[0].nbytes,
+                "mode": "pipelined: uploads/downloads on copy streams overlap the next/previous "
+                        "step's NS",
+                "serial_ms_per_step": round(serial_ms, 4),
+                "serial_value": round(flops / (serial_ms * 1e-3) / 1e12, 2)},
+        "launches": launches,
         "extra": dict(extra, torch_eager_gpu_ms=round(eager_ms, 4),
                       speedup_vs_torch_eager_gpu=round(eager_ms / ms, 3)),
     }
@@ -363,6 +415,7 @@ def bench_ns(args, peaks, peak_src):
 
 def bench_muon(args, world, rank, peaks, peak_src):
     from muon_fused import FusedMuon, _lib
+    from muon_fused.sharding import ShardPlan
 
     dev = torch.device("cuda")
     shapes = llama_shapes(args.workload)
@@ -379,27 +432,100 @@ def bench_muon(args, world, rank, peaks, peak_src):
         opt.step()
     torch.cuda.synchronize()
     stream = torch.cuda.current_stream()
-    if world > 1:
-        import torch.distributed as dist
 
-        dist.barrier()
-    torch.cuda.synchronize()
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    barrier()
     s_ev, e_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n_launch0 = _lib.launch_count()
     with ClockSampler(torch.cuda.current_device()) as clk:
         s_ev.record(stream)
         for _ in range(args.steps):
             opt.step()
         e_ev.record(stream)
         torch.cuda.synchronize()
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.barrier()
-    ms = s_ev.elapsed_time(e_ev) / args.steps
-    ms = barrier_max(ms, world)
+    launches = _lib.launch_count() - n_launch0
+    barrier()
+    ms = barrier_max(s_ev.elapsed_time(e_ev) / args.steps, world)
     flops = sum(ns_flops(*s) for s in shapes)
-    return {"ms": ms, "flops": flops, "roofline": None, "clocks": clk.summary(), "e2e": None,
-            "launches": None, "extra": {"matrices": len(shapes)}}
+
+    # GEMM3 roofline: per-launch events over a few steps; FLOPs of the
+    # matrices this rank owns (all of them at N = 1).
+    owner = ShardPlan.assign([tuple(s) for s in shapes], world) if world > 1 else [0] * len(shapes)
+    mine = [s for s, o in zip(shapes, owner) if o == rank]
+    prof_steps = 3
+    _lib.stage_timing(True)
+    for _ in range(prof_steps):
+        opt.step()
+    st = _lib.stage_times()
+    _lib.stage_timing(False)
+    barrier()
+    g3_flops = prof_steps * NS_STEPS * sum(2.0 * min(s) ** 2 * max(s) for s in mine)
+    g3_ms = st["gemm3_bx"][0]
+    achieved = g3_flops / (g3_ms * 1e-3) / 1e12 if g3_ms > 0 else 0.0
+    peak = float(peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"]))
+    total = sum(v[0] for v in st.values())
+    roofline = {"bound": "tensor", "kernel": "ns_gemm_pair_kernel<kBX> (X' = d*X + Boff*X), batched",
+                "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
+                "frac": round(achieved / peak, 4),
+                "peak_source": f"{peak_src} bf16_tflops_sustained (kernel timed inside a long step)",
+                "traffic": None, "rank": rank,
+                "stages": {k: {"launches": c, "ms_per_step": round(t / prof_steps, 3),
+                               "share_of_ns_time": round(t / total, 4) if total else 0.0}
+                           for k, (t, c) in st.items() if c}}
+
+    # End to end: every step uploads the gradients of the matrices this rank
+    # owns (the only ones its step reads) from pinned host memory and reads
+    # two bytes of the updated parameters back; uploads for step i+1 run on a
+    # copy stream, into the second of two device gradient sets, during step i.
+    own = [p for p, o in zip(params, owner) if o == rank]
+    host = [p.grad.detach().cpu().pin_memory() for p in own]
+    sets = [[p.grad for p in own], [torch.empty_like(p.grad) for p in own]]
+    probe = torch.empty(1, dtype=torch.bfloat16).pin_memory()
+    up = torch.cuda.Stream()
+    uploaded = [torch.cuda.Event() for _ in range(2)]
+    stepped = [torch.cuda.Event() for _ in range(2)]
+    e2e_steps = max(3, min(args.steps, 20))
+    barrier()
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record(stream)
+    up.wait_stream(stream)
+    with torch.cuda.stream(up):
+        for d, h in zip(sets[0], host):
+            d.copy_(h, non_blocking=True)
+        uploaded[0].record(up)
+    for i in range(e2e_steps):
+        b = i & 1
+        stream.wait_event(uploaded[b])
+        for p, d in zip(own, sets[b]):
+            p.grad = d
+        opt.step()
+        stepped[b].record(stream)
+        probe.copy_(params[-1].detach().view(-1)[:1], non_blocking=True)
+        if i + 1 < e2e_steps:
+            with torch.cuda.stream(up):
+                if i >= 1:
+                    up.wait_event(stepped[b ^ 1])  # step i-1 has read that set
+                for d, h in zip(sets[b ^ 1], host):
+                    d.copy_(h, non_blocking=True)
+                uploaded[b ^ 1].record(up)
+    e2.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = barrier_max(s2.elapsed_time(e2) / e2e_steps, world)
+    h2d = sum(h.nbytes for h in host)
+    e2e = {"value": round(flops / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+           "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": h2d,
+           "d2h_bytes_per_step": probe.nbytes, "steps": e2e_steps,
+           "mode": "pipelined: owned gradients uploaded from pinned host memory on a copy "
+                   "stream during the previous step; rank 0's bytes"}
+    return {"ms": ms, "flops": flops, "roofline": roofline, "clocks": clk.summary(), "e2e": e2e,
+            "launches": launches, "extra": {"matrices": len(shapes)}}
 
 
 def main():

@@ -230,6 +230,14 @@ int fm_set_gemm_path(int path);
 int fm_stage_timing(int enable);
 int fm_stage_times(float* ms, int* counts);
 
+/*
+ * Number of kernels this library has launched in the calling process since it
+ * was loaded (all devices, all threads); a benchmark reads it before and after
+ * its timed region.
+ * Replaces: nothing (benchmark instrumentation).
+ */
+int fm_launch_count(uint64_t* count);
+
 #ifdef __cplusplus
 }
 #endif

@@ -47,6 +47,7 @@ SIGNATURES = {
     "fm_set_gemm_path": (_c_int, [_c_int]),
     "fm_stage_timing": (_c_int, [_c_int]),
     "fm_stage_times": (_c_int, [ctypes.POINTER(ctypes.c_float), ctypes.POINTER(_c_int)]),
+    "fm_launch_count": (_c_int, [ctypes.POINTER(ctypes.c_uint64)]),
 }
 
 _lib = None
@@ -115,6 +116,13 @@ def stage_times():
     cnt = (ctypes.c_int * 4)()
     check(load().fm_stage_times(ms, cnt), "fm_stage_times")
     return {STAGES[i]: (float(ms[i]), int(cnt[i])) for i in range(4)}
+
+
+def launch_count() -> int:
+    """Kernels the library has launched in this process (see fm_launch_count)."""
+    n = ctypes.c_uint64(0)
+    check(load().fm_launch_count(ctypes.byref(n)), "fm_launch_count")
+    return int(n.value)
 
 
 def set_gemm_path(path: int) -> None:

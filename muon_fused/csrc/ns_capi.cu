@@ -179,6 +179,10 @@ int make_map(CUtensorMap* map, const void* base, long long batch, long long rows
 // batches and once the matrix spans more than one 256-row block.
 std::atomic<int> g_gemm_path{0};
 
+// Kernels this library has launched in the process (fm_launch_count).
+std::atomic<unsigned long long> g_launches{0};
+inline void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
 // CTA pairs of a 148-SM B200.  Split-K choices (and therefore workspace
 // sizes) are made against this constant so fm_workspace_size needs no device.
 constexpr int kRefPairs = 74;
@@ -300,7 +304,9 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
   }
   cfg.attrs = attr;
   cfg.numAttrs = n;
-  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+  if (e == cudaSuccess) note_launch();
+  return e;
 }
 
 template <int MODE>
@@ -558,6 +564,7 @@ static int step_common(const void* X, int64_t m, int64_t n, int64_t ldx, void* X
     scale_kernel<<<dim3(pg, 1), kPrepThreads, 0, st>>>(X, FM_DT_BF16, m, n, ldx, 0, nullptr, 0,
                                                       w.X[0], w.ldx, w.xs);
     FM_CUDA(cudaGetLastError());
+    note_launch();
     io.cur = w.X[0];
     io.ldc = w.ldx;
   }
@@ -624,6 +631,7 @@ int fm_muon_momentum(void* buf, const void* grad, void* dir, int64_t n, int dtyp
       return fail(FM_E_INVALID, "fm_muon_momentum: unsupported dtype %d", dtype);
   }
   FM_CUDA(cudaGetLastError());
+  note_launch();
   return FM_OK;
 }
 
@@ -654,6 +662,7 @@ int fm_muon_apply(void* param, int dtype, const void* update, int64_t n, float d
       return fail(FM_E_INVALID, "fm_muon_apply: unsupported dtype %d", dtype);
   }
   FM_CUDA(cudaGetLastError());
+  note_launch();
   return FM_OK;
 }
 
@@ -694,6 +703,7 @@ int fm_peer_signal(int64_t* flag, int64_t value, void* stream) {
   peer_signal_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(
       reinterpret_cast<long long*>(flag), static_cast<long long>(value));
   FM_CUDA(cudaGetLastError());
+  note_launch();
   return FM_OK;
 }
 
@@ -709,6 +719,7 @@ int fm_peer_gather_apply(const fm_apply_entry* entries, int nentries, const void
       reinterpret_cast<const long long* const*>(peer_flags), flag_index,
       static_cast<long long>(expected), ds->err_word);
   FM_CUDA(cudaGetLastError());
+  note_launch();
   return FM_OK;
 }
 
@@ -722,6 +733,12 @@ int fm_stage_timing(int enable) {
   t_timer.on = enable != 0;
   t_timer.used = 0;
   t_timer.marks.clear();
+  return FM_OK;
+}
+
+int fm_launch_count(uint64_t* count) {
+  if (!count) return fail(FM_E_INVALID, "null pointer argument");
+  *count = g_launches.load(std::memory_order_relaxed);
   return FM_OK;
 }
 
