@@ -421,8 +421,13 @@ int check_dims(long long rows, long long cols) {
   return FM_OK;
 }
 
-int prep_grid(long long rows, const DeviceState& ds) {
-  return int(std::min<long long>(std::min<long long>(rows, kMaxPartials), ds.sm_count * 4));
+// Blocks of the norm / scale kernels: one per kPrepThreads * kFlatUnroll
+// chunks, at most four per SM and kMaxPartials (the partials of one matrix).
+int prep_grid(long long rows, long long cols, const DeviceState& ds) {
+  const long long chunks = rows * ((cols + 7) / 8);
+  const long long want = (chunks + kPrepThreads * kFlatUnroll - 1) / (kPrepThreads * kFlatUnroll);
+  const long long cap = std::min<long long>(kMaxPartials, ds.sm_count * 4ll);
+  return int(std::max<long long>(1, std::min(want, cap)));
 }
 
 // Full Newton-Schulz over a batch of same-shape matrices (batch = 1 for the
@@ -451,7 +456,7 @@ int ns_run(const void* G, int dtype, long long batch, long long rows, long long 
   const NsPlan P = plan_ns(batch, m, n, g_gemm_path.load(std::memory_order_relaxed));
   auto* o = static_cast<__nv_bfloat16*>(out);
 
-  const int pg = prep_grid(rows, *ds);
+  const int pg = prep_grid(rows, cols, *ds);
   const long long tm = timer_begin(3, st);
   if (P.split_slots > 0) FM_CUDA(cudaMemsetAsync(w.counters, 0, w.counter_bytes, st));
   const long long bs_g_eff = batch > 1 ? bs_g : 0;
@@ -560,7 +565,7 @@ static int step_common(const void* X, int64_t m, int64_t n, int64_t ldx, void* X
   io.cur_bs = 0;
   if ((reinterpret_cast<uintptr_t>(X) & 15) != 0 || ldx % 8 != 0) {
     // Not TMA-addressable: copy into the workspace (no normalisation).
-    const int pg = prep_grid(m, *ds);
+    const int pg = prep_grid(m, n, *ds);
     scale_kernel<<<dim3(pg, 1), kPrepThreads, 0, st>>>(X, FM_DT_BF16, m, n, ldx, 0, nullptr, 0,
                                                       w.X[0], w.ldx, w.xs);
     FM_CUDA(cudaGetLastError());

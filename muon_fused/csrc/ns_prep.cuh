@@ -27,6 +27,7 @@ enum : int { kDtBF16 = 0, kDtF16 = 1, kDtF32 = 2, kDtF64 = 3 };
 constexpr int kPrepThreads = 256;
 constexpr int kMaxPartials = 1024;
 constexpr int kUnroll = 4;
+constexpr int kFlatUnroll = 8;  // 16-byte loads in flight per thread on the flat path
 
 // Value of G[i] after the reference's cast to bf16, widened to fp32.
 __device__ __forceinline__ float load_bf16_rounded(const void* G, int dtype, long long i) {
@@ -80,6 +81,55 @@ struct ChunkGrid {
   }
 };
 
+// Per-thread walk over a block's (row, chunk) pairs.  Thread t visits the
+// linear indices t + u*blockDim.x + j*kUnroll*blockDim.x (u < kUnroll) of the
+// block's row-major chunk range, as a plain linear loop would; the row/chunk
+// split of each index is advanced by a precomputed step instead of a 64-bit
+// divide per chunk (which made these kernels ALU-bound).
+struct ChunkWalk {
+  long long r[kUnroll];
+  int c[kUnroll];
+  int chunks, step_r, step_c;
+  __device__ __forceinline__ void init(long long r0, long long nchunks) {
+    chunks = static_cast<int>(nchunks);
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int i = static_cast<int>(threadIdx.x + u * blockDim.x);
+      r[u] = r0 + i / chunks;
+      c[u] = i % chunks;
+    }
+    const int step = kUnroll * static_cast<int>(blockDim.x);
+    step_r = step / chunks;
+    step_c = step % chunks;
+  }
+  __device__ __forceinline__ void advance() {
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      c[u] += step_c;
+      r[u] += step_r;
+      if (c[u] >= chunks) {
+        c[u] -= chunks;
+        ++r[u];
+      }
+    }
+  }
+};
+
+// bf16(fl32(x / den)) from rcp = fl32(1 / den) without a full division per
+// element.  q = fl32(x * rcp) is within 3 fp32 ulps of fl32(x / den) (two
+// roundings of at most half an ulp each, plus the quotient's own rounding),
+// i.e. within 6 steps of the bit pattern even across a binade edge; both round
+// to the same bf16 unless a bf16 rounding midpoint (low 16 bits == 0x8000)
+// lies between them.  So q is used unless its low half is within 16 patterns
+// of 0x8000, where the exact division decides (Ziv's strategy: a cheap
+// approximation, a rounding test, an exact fallback for the rare hard case).
+// Also exact for zeros, infinities, NaNs and subnormal quotients.
+__device__ __forceinline__ float div_for_bf16(float x, float den, float rcp) {
+  const float q = x * rcp;
+  const int low = static_cast<int>(__float_as_uint(q) & 0xFFFFu);
+  return abs(low - 0x8000) <= 16 ? x / den : q;
+}
+
 // Load chunk (r, c) as bf16-rounded floats (zero beyond cols).
 __device__ __forceinline__ void load_chunk(const void* G, int dtype, const ChunkGrid& g, bool vec,
                                            long long r, long long c, float (&x)[8]) {
@@ -102,39 +152,21 @@ __device__ __forceinline__ bool bf16_vec_ok(const void* p, int dtype, long long 
   return dtype == kDtBF16 && ((reinterpret_cast<uintptr_t>(p) | static_cast<uintptr_t>(ld * 2)) & 15) == 0;
 }
 
-// partials[b][blockIdx.x] = sum over this block's rows of bf16(G_b)^2 (fp32);
-// blockIdx.y = b, the matrix of the batch (element stride bs_g).
-__global__ void __launch_bounds__(kPrepThreads) sumsq_kernel(const void* __restrict__ G0, int dtype,
-                                                             long long rows, long long cols,
-                                                             long long ldg, long long bs_g,
-                                                             float* partials) {
-  pdl_wait();
-  const void* G = batch_ptr(G0, dtype, bs_g, blockIdx.y);
-  partials += static_cast<long long>(blockIdx.y) * kMaxPartials;
-  const ChunkGrid g{rows, cols, ldg, (cols + 7) / 8};
-  const bool vec = bf16_vec_ok(G, dtype, ldg);
-  long long r0, r1;
-  g.block_rows(r0, r1);
-  const long long total = (r1 - r0) * g.chunks;
-  float acc = 0.f;
-  for (long long i0 = threadIdx.x; i0 < total; i0 += kUnroll * blockDim.x) {
-    float x[kUnroll][8];
-#pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      const long long i = i0 + u * blockDim.x;
-      if (i < total) {
-        const long long r = r0 + i / g.chunks, c = i % g.chunks;
-        load_chunk(G, dtype, g, vec, r, c, x[u]);
-      } else {
-#pragma unroll
-        for (int k = 0; k < 8; ++k) x[u][k] = 0.f;
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < kUnroll; ++u)
-#pragma unroll
-      for (int k = 0; k < 8; ++k) acc = fmaf(x[u][k], x[u][k], acc);
-  }
+// A bf16 matrix stored as one dense run of 16-byte chunks (row stride ==
+// cols, cols a multiple of 8, 16-byte aligned): the prep kernels then walk a
+// flat chunk array.  Block b of the grid owns chunks [lo, hi) of it.
+__device__ __forceinline__ bool flat_ok(const void* p, int dtype, long long cols, long long ld) {
+  return bf16_vec_ok(p, dtype, ld) && ld == cols && (cols & 7) == 0;
+}
+
+__device__ __forceinline__ void flat_range(long long total, long long& lo, long long& hi) {
+  const long long per = (total + gridDim.x - 1) / gridDim.x;
+  lo = min(total, per * blockIdx.x);
+  hi = min(total, lo + per);
+}
+
+// partials[blockIdx.x] = the block's sum of `acc` (warps in a fixed order).
+__device__ __forceinline__ void block_sum_store(float acc, float* partials) {
   __shared__ float red[kPrepThreads / 32];
   acc = warp_sum(acc);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
@@ -144,6 +176,67 @@ __global__ void __launch_bounds__(kPrepThreads) sumsq_kernel(const void* __restr
     v = warp_sum(v);
     if (threadIdx.x == 0) partials[blockIdx.x] = v;
   }
+}
+
+// partials[b][blockIdx.x] = sum over this block's part of bf16(G_b)^2 (fp32);
+// blockIdx.y = b, the matrix of the batch (element stride bs_g).
+__global__ void __launch_bounds__(kPrepThreads, 4) sumsq_kernel(const void* __restrict__ G0, int dtype,
+                                                             long long rows, long long cols,
+                                                             long long ldg, long long bs_g,
+                                                             float* partials) {
+  pdl_wait();
+  const void* G = batch_ptr(G0, dtype, bs_g, blockIdx.y);
+  partials += static_cast<long long>(blockIdx.y) * kMaxPartials;
+  const ChunkGrid g{rows, cols, ldg, (cols + 7) / 8};
+  const bool vec = bf16_vec_ok(G, dtype, ldg);
+  float acc = 0.f;
+  if (flat_ok(G, dtype, cols, ldg)) {
+    // Raw 16-byte loads first (4 registers each), so that kFlatUnroll of them
+    // are in flight per thread at the register budget of four blocks per SM.
+    const uint4* src = static_cast<const uint4*>(G);
+    long long lo, hi;
+    flat_range(rows * g.chunks, lo, hi);
+    for (long long l0 = lo + threadIdx.x; l0 < hi; l0 += kFlatUnroll * blockDim.x) {
+      uint4 raw[kFlatUnroll];
+#pragma unroll
+      for (int u = 0; u < kFlatUnroll; ++u) {
+        const long long l = l0 + u * static_cast<long long>(blockDim.x);
+        raw[u] = l < hi ? __ldg(src + l) : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int u = 0; u < kFlatUnroll; ++u) {
+        float x[8];
+        unpack8(raw[u], x);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) acc = fmaf(x[k], x[k], acc);
+      }
+    }
+    block_sum_store(acc, partials);
+    pdl_trigger();
+    return;
+  }
+  long long r0, r1;
+  g.block_rows(r0, r1);
+  ChunkWalk w;
+  w.init(r0, g.chunks);
+  while (w.r[0] < r1) {
+    float x[kUnroll][8];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      if (w.r[u] < r1) {
+        load_chunk(G, dtype, g, vec, w.r[u], w.c[u], x[u]);
+      } else {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) x[u][k] = 0.f;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u)
+#pragma unroll
+      for (int k = 0; k < 8; ++k) acc = fmaf(x[u][k], x[u][k], acc);
+    w.advance();
+  }
+  block_sum_store(acc, partials);
   pdl_trigger();
 }
 
@@ -162,7 +255,7 @@ __device__ __forceinline__ float norm_denominator(const float* partials, int npa
 // X[r][c] = bf16(bf16(G[r][c]) / (||G|| + 1e-7)), same layout as G;
 // blockIdx.y = matrix of the batch (element strides bs_g in, xs out).
 // With nparts == 0 no normalisation is applied (plain cast/copy).
-__global__ void __launch_bounds__(kPrepThreads) scale_kernel(const void* __restrict__ G0, int dtype,
+__global__ void __launch_bounds__(kPrepThreads, 4) scale_kernel(const void* __restrict__ G0, int dtype,
                                                              long long rows, long long cols,
                                                              long long ldg, long long bs_g,
                                                              const float* partials, int nparts,
@@ -177,23 +270,49 @@ __global__ void __launch_bounds__(kPrepThreads) scale_kernel(const void* __restr
   const ChunkGrid g{rows, cols, ldg, (cols + 7) / 8};
   const bool vin = bf16_vec_ok(G, dtype, ldg);
   const bool vout = ((reinterpret_cast<uintptr_t>(X) | static_cast<uintptr_t>(ldx * 2)) & 15) == 0;
+  const float rcp = 1.f / den;
+  if (vout && ldx == cols && flat_ok(G, dtype, cols, ldg)) {
+    const uint4* src = static_cast<const uint4*>(G);
+    uint4* dst = reinterpret_cast<uint4*>(X);
+    long long lo, hi;
+    flat_range(rows * g.chunks, lo, hi);
+    for (long long l0 = lo + threadIdx.x; l0 < hi; l0 += kFlatUnroll * blockDim.x) {
+      uint4 raw[kFlatUnroll];
+#pragma unroll
+      for (int u = 0; u < kFlatUnroll; ++u) {
+        const long long l = l0 + u * static_cast<long long>(blockDim.x);
+        if (l < hi) raw[u] = __ldg(src + l);
+      }
+#pragma unroll
+      for (int u = 0; u < kFlatUnroll; ++u) {
+        const long long l = l0 + u * static_cast<long long>(blockDim.x);
+        if (l >= hi) continue;
+        float x[8];
+        unpack8(raw[u], x);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) x[k] = div_for_bf16(x[k], den, rcp);
+        dst[l] = pack8(x);
+      }
+    }
+    pdl_trigger();
+    return;
+  }
   long long r0, r1;
   g.block_rows(r0, r1);
-  const long long total = (r1 - r0) * g.chunks;
-  for (long long i0 = threadIdx.x; i0 < total; i0 += kUnroll * blockDim.x) {
+  ChunkWalk w;
+  w.init(r0, g.chunks);
+  for (; w.r[0] < r1; w.advance()) {
     float x[kUnroll][8];
 #pragma unroll
     for (int u = 0; u < kUnroll; ++u) {
-      const long long i = i0 + u * blockDim.x;
-      if (i < total) load_chunk(G, dtype, g, vin, r0 + i / g.chunks, i % g.chunks, x[u]);
+      if (w.r[u] < r1) load_chunk(G, dtype, g, vin, w.r[u], w.c[u], x[u]);
     }
 #pragma unroll
     for (int u = 0; u < kUnroll; ++u) {
-      const long long i = i0 + u * blockDim.x;
-      if (i >= total) continue;
-      const long long r = r0 + i / g.chunks, c = i % g.chunks;
+      if (w.r[u] >= r1) continue;
+      const long long r = w.r[u], c = w.c[u];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) x[u][k] = x[u][k] / den;
+      for (int k = 0; k < 8; ++k) x[u][k] = div_for_bf16(x[u][k], den, rcp);
       __nv_bfloat16* dst = X + r * ldx + c * 8;
       if (vout && c * 8 + 8 <= cols) {
         *reinterpret_cast<uint4*>(dst) = pack8(x[u]);
@@ -209,7 +328,12 @@ __global__ void __launch_bounds__(kPrepThreads) scale_kernel(const void* __restr
 
 // Transposing variant for tall G (rows > cols): X[c][r] = bf16(bf16(G[r][c]) / den).
 // 64x64 tiles through shared memory so both the read and the write coalesce.
+// Each thread issues both of its row-chunk loads before using either.  The
+// tile's row pitch of 66 elements (33 words) keeps the column-wise gathers of
+// the store phase to at most two-way bank conflicts (a pitch of 72 made them
+// eight-way) and the row-wise writes of the load phase conflict-free.
 constexpr int kTT = 64;
+constexpr int kTPitchT = kTT + 2;
 __global__ void __launch_bounds__(kPrepThreads) scale_transpose_kernel(
     const void* __restrict__ G0, int dtype, long long rows, long long cols, long long ldg,
     long long bs_g, const float* partials, int nparts, __nv_bfloat16* X, long long ldx,
@@ -219,30 +343,41 @@ __global__ void __launch_bounds__(kPrepThreads) scale_transpose_kernel(
   partials += static_cast<long long>(blockIdx.z) * kMaxPartials;
   X += static_cast<long long>(blockIdx.z) * xs;
   __shared__ float s_den;
-  __shared__ __align__(16) __nv_bfloat16 tile[kTT][kTT + 8];
+  __shared__ __nv_bfloat16 tile[kTT][kTPitchT];
   const float den = nparts > 0 ? norm_denominator(partials, nparts, &s_den) : 1.f;
+  const float rcp = 1.f / den;
   const ChunkGrid g{rows, cols, ldg, (cols + 7) / 8};
   const bool vin = bf16_vec_ok(G, dtype, ldg);
   const bool vout = ((reinterpret_cast<uintptr_t>(X) | static_cast<uintptr_t>(ldx * 2)) & 15) == 0;
   const long long r0 = static_cast<long long>(blockIdx.y) * kTT;
   const long long c0 = static_cast<long long>(blockIdx.x) * kTT;
-  // load: 64 rows x 8 chunks, two per thread
-  for (int i = threadIdx.x; i < kTT * (kTT / 8); i += kPrepThreads) {
-    const int tr = i / (kTT / 8), tc = i % (kTT / 8);
-    const long long r = r0 + tr, cc = c0 / 8 + tc;
-    float x[8];
+  constexpr int kPer = kTT * (kTT / 8) / kPrepThreads;  // row chunks per thread (2)
+  // load: 64 rows x 8 chunks
+  float x[kPer][8];
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const int i = threadIdx.x + j * kPrepThreads;
+    const long long r = r0 + i / (kTT / 8), cc = c0 / 8 + i % (kTT / 8);
     if (r < rows) {
-      load_chunk(G, dtype, g, vin, r, cc, x);
+      load_chunk(G, dtype, g, vin, r, cc, x[j]);
     } else {
 #pragma unroll
-      for (int k = 0; k < 8; ++k) x[k] = 0.f;
+      for (int k = 0; k < 8; ++k) x[j][k] = 0.f;
     }
+  }
 #pragma unroll
-    for (int k = 0; k < 8; ++k) tile[tr][tc * 8 + k] = __float2bfloat16_rn(x[k] / den);
+  for (int j = 0; j < kPer; ++j) {
+    const int i = threadIdx.x + j * kPrepThreads;
+    const int tr = i / (kTT / 8), tc = i % (kTT / 8);
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      tile[tr][tc * 8 + k] = __float2bfloat16_rn(div_for_bf16(x[j][k], den, rcp));
   }
   __syncthreads();
   // store: output rows c0.. (64 of them) x 8 chunks along r
-  for (int i = threadIdx.x; i < kTT * (kTT / 8); i += kPrepThreads) {
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const int i = threadIdx.x + j * kPrepThreads;
     const int orow = i / (kTT / 8), oc = i % (kTT / 8);
     const long long c = c0 + orow;  // output row
     const long long r = r0 + oc * 8;  // first output column

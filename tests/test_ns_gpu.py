@@ -225,3 +225,25 @@ def test_orthogonality_property_full_size(cuda_lib):
                     dtype=torch.bfloat16)
     s = torch.linalg.svdvals(_ns(G).float())
     assert s.min() > 0.5 and s.max() < 1.3
+
+
+@pytest.mark.parametrize("batch,rows,cols,kmax", [(64, 96, 128, 32), (4, 256, 1024, 8),
+                                                  (3, 200, 72, 16)])
+def test_normalisation_bit_exact(cuda_lib, batch, rows, cols, kmax):
+    """steps=0 returns the normalised input bf16(bf16(G) / (||G||_F + 1e-7)).
+    Entries k/32 with |k| <= kmax keep every partial sum of squares exact in
+    fp32, so the denominator is known exactly and the output must equal an
+    IEEE fp32 division rounded to bf16, element for element; this covers the
+    kernels' reciprocal fast path and its exact-division fallback near bf16
+    rounding midpoints."""
+    from muon_fused import _fused_muon_C as _C
+
+    g = torch.Generator().manual_seed(rows * cols + kmax)
+    k = torch.randint(-kmax, kmax + 1, (batch, rows, cols), generator=g)
+    G = (k.double() / 32).to(torch.bfloat16)
+    out = _C.fused_newton_schulz_batched(G.to(DEV), 0).cpu()
+    for b in range(batch):
+        s = float((G[b].double() ** 2).sum())
+        den = torch.sqrt(torch.tensor(s, dtype=torch.float32)) + 1e-7
+        ref = (G[b].float() / den).to(torch.bfloat16)
+        assert torch.equal(out[b], ref), b
