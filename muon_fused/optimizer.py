@@ -16,8 +16,9 @@ B200-specific behaviour:
   under ``torch.distributed`` with world size > 1 each rank orthogonalises
   only the matrices it owns (FLOP-balanced assignment) and the bf16 updates
   are all-gathered over NCCL; with one process everything is local.
-* Momentum state is kept only by the owning rank (``state_dict`` is therefore
-  rank-local when sharded; keys are the reference's ``momentum_buffer``).
+* Momentum state is kept only by the owning rank, so ``state_dict`` is
+  rank-local when sharded until ``consolidate_state_dict()`` broadcasts every
+  buffer from its owner; keys are the reference's ``momentum_buffer``.
 """
 
 from __future__ import annotations
@@ -99,6 +100,9 @@ class FusedMuon(Optimizer):
             raise ValueError(f"collective must be 'nccl' or 'peer', got {collective!r}")
         self._collective = collective
         self._exchanges: dict[tuple, Any] = {}
+        # id(group) -> (params, owner rank per param, momentum dtype per param)
+        # of the group's last sharded step (consolidate_state_dict)
+        self._owners: dict[int, tuple] = {}
 
     # ------------------------------------------------------------------ helpers
     @staticmethod
@@ -243,6 +247,11 @@ class FusedMuon(Optimizer):
                                             self._bucket_bytes)
             self._plans[key] = plan
 
+        self._owners[id(group)] = (params, list(plan.owner), [p.grad.dtype for p in params])
+        for p, r in zip(params, plan.owner):
+            if r != rank and p in self.state:  # e.g. after loading a consolidated checkpoint
+                self.state[p].pop("momentum_buffer", None)
+
         def compute(indices, out) -> None:
             rows, cols = out.shape[1], out.shape[2]
             lim = self._batch_limit(rows, cols)
@@ -305,6 +314,39 @@ class FusedMuon(Optimizer):
 
     # ------------------------------------------------------------------ step
     @torch.no_grad()
+    def consolidate_state_dict(self) -> None:
+        """Make every rank's optimizer state complete after sharded steps.
+
+        Under sharding a matrix's momentum buffer lives only on the rank that
+        owns it.  This broadcasts every buffer from its owner, so that
+        ``state_dict()`` on any rank then holds the same keys and values as a
+        single-process run (and as the reference optimizer,
+        optimizer.py:140-141): ready to save, and to load into a run with any
+        number of ranks (a sharded step keeps only the buffers its rank owns).
+        A collective: every rank of the process group calls it.  Without
+        sharding it does nothing.
+        """
+        pg, rank, world = self._world()
+        if world <= 1:
+            return
+        import torch.distributed as dist
+
+        for group in self.param_groups:
+            rec = self._owners.get(id(group))
+            if rec is None:
+                continue
+            params, owner, dtypes = rec
+            for p, r, dt in zip(params, owner, dtypes):
+                st = self.state[p]
+                buf = st.get("momentum_buffer") if r == rank else None
+                if buf is None:
+                    # the buffer has the gradient's 2-D view shape (see _orthogonalise_batch)
+                    shape = (p.shape[0], p.numel() // p.shape[0]) if p.ndim > 2 else p.shape
+                    buf = torch.empty(shape, dtype=dt, device=p.device)
+                    st["momentum_buffer"] = buf
+                src = dist.get_global_rank(pg, r) if pg is not None else r
+                dist.broadcast(buf, src=src, group=pg)
+
     def step(self, closure=None):
         """One optimisation step (optimizer.py:99-202)."""
         loss = None

@@ -5,9 +5,11 @@ oracle's fp32 restatement so the sharding logic (owner table, momentum
 ownership, bucketed all-gather, apply order) runs without CUDA.  Checks:
 identical parameters on every rank, equal to a single-process run; balanced
 and deterministic owner tables; uneven shards; a rank that leaves between
-steps surfaces as an error on the others.
+steps surfaces as an error on the others; a consolidated checkpoint equals the
+single-process state and resumes to the single-process trajectory.
 """
 
+import copy
 import os
 import socket
 import tempfile
@@ -164,3 +166,57 @@ def test_rank_leaving_between_steps_is_an_error():
     assert not os.path.exists(os.path.join(outdir, "rank0.pt"))
     with open(os.path.join(outdir, "rank0.err")) as f:
         assert f.read()
+
+
+def _ckpt_worker(rank, world, port, outdir):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import datetime
+
+    from muon_fused import FusedMuon
+
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=30))
+    _patch_ns()
+    try:
+        params = _make()
+        opt = _run_steps(params, 2, 8192)
+        opt.consolidate_state_dict()
+        sd = copy.deepcopy(opt.state_dict())  # as saved to disk: no tensors shared with opt
+        # resume: a fresh sharded optimizer loads the checkpoint, runs step 3
+        opt2 = FusedMuon([{"params": params, "use_muon": True}], lr=0.02, bucket_bytes=8192)
+        opt2.load_state_dict(copy.deepcopy(sd))  # load_state_dict keeps the given tensors
+        for p, g in zip(params, _grads(2)):
+            p.grad = g.clone()
+        opt2.step()
+        kept = sorted(i for i, p in enumerate(params) if "momentum_buffer" in opt2.state[p])
+        torch.save({"state": sd["state"], "params": [p.detach() for p in params], "kept": kept},
+                   os.path.join(outdir, f"rank{rank}.pt"))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_consolidated_checkpoint_matches_single_process_and_resumes(world):
+    _patch_ns()
+    params = _make()
+    opt = _run_steps(params, 2, 1 << 30)
+    ref_state = copy.deepcopy(opt.state_dict()["state"])  # step 3 below updates buffers in place
+    for p, g in zip(params, _grads(2)):
+        p.grad = g.clone()
+    opt.step()
+    ref_params = [p.detach() for p in params]
+    outdir = tempfile.mkdtemp()
+    mp.spawn(_ckpt_worker, args=(world, _free_port(), outdir), nprocs=world, join=True)
+    kept = []
+    for r in range(world):
+        res = torch.load(os.path.join(outdir, f"rank{r}.pt"))
+        # every rank's consolidated state has every buffer, equal to one process's
+        assert sorted(res["state"]) == sorted(ref_state)
+        for k, v in ref_state.items():
+            assert torch.equal(res["state"][k]["momentum_buffer"], v["momentum_buffer"])
+        for a, b in zip(res["params"], ref_params):
+            assert torch.equal(a, b)
+        kept += res["kept"]
+    # after the resumed step each buffer is kept by its owner only
+    assert sorted(kept) == list(range(len(SHAPES)))
