@@ -41,8 +41,10 @@ def _run(params, device, steps=3, collective="nccl"):
         for p, g in zip(params, _grads(s, device)):
             p.grad = g
         opt.step()
+    opt.consolidate_state_dict()  # no-op on one process
     torch.cuda.synchronize(device)
-    return [p.detach().cpu() for p in params]
+    moms = [opt.state[p]["momentum_buffer"].cpu() for p in params]
+    return [p.detach().cpu() for p in params], moms
 
 
 def _worker(rank, world, port, outdir, collective):
@@ -70,10 +72,12 @@ def test_sharded_nccl_matches_single_gpu(cuda_lib):
     """Both exchanges (NCCL all-gather; fused peer-memory gather + apply over
     NVLink) give every rank the same parameters, bit-identical between the
     two exchanges, and equal to the single-GPU run up to summation order.
-    Three steps exercise both parities of the peer send buffers."""
+    Three steps exercise both parities of the peer send buffers.  After
+    consolidate_state_dict() every rank holds every momentum buffer, equal to
+    the single-GPU run's."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
-    ref = _run(_params(torch.device("cuda", 0)), torch.device("cuda", 0))
+    ref, ref_mom = _run(_params(torch.device("cuda", 0)), torch.device("cuda", 0))
     outdir = tempfile.mkdtemp()
     for collective in ("nccl", "peer"):
         mp.spawn(_worker, args=(2, _port(), outdir, collective), nprocs=2, join=True)
@@ -83,8 +87,13 @@ def test_sharded_nccl_matches_single_gpu(cuda_lib):
     got = {c: [torch.load(os.path.join(outdir, f"{c}{r}.pt")) for r in range(2)]
            for c in ("nccl", "peer")}
     for c in got:
-        for a, b in zip(got[c][0], got[c][1]):
+        for a, b in zip(got[c][0][0], got[c][1][0]):
             assert torch.equal(a, b)  # every rank applied the same updates
+        for r in range(2):
+            # consolidated momentum state on every rank equals the single-GPU run's
+            for a, b in zip(got[c][r][1], ref_mom):
+                assert torch.equal(a, b)
+    got = {c: [v[0] for v in got[c]] for c in got}
     for a, b in zip(got["nccl"][0], got["peer"][0]):
         assert torch.equal(a, b)  # same arithmetic, different transport
     # Batches differ between the sharded and the single-GPU run (so may the
