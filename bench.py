@@ -531,7 +531,9 @@ def bench_muon(args, world, rank, peaks, peak_src):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--steps", type=int, default=None,
+                    help="timed steps (default: 400 for ns, 40 for the optimizer-step workloads, "
+                         "so the timed work stays within about a minute)")
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--workload", choices=["ns", "muon1b", "muon8b"], default=None)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
@@ -548,6 +550,8 @@ def main():
     world, rank, local = dist_env()
     if args.workload is None:
         args.workload = "ns" if world == 1 else "muon8b"
+    if args.steps is None:
+        args.steps = 400 if args.workload == "ns" else 40
     args.warmup = max(args.warmup, 3)
 
     if args.impl == "reference":
