@@ -1,18 +1,25 @@
 """Benchmark of the Newton-Schulz / Muon hot path on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload ns|muon1b|muon8b]
-                    [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W]
+                    [--workload muon8b|muon1b|ns|sweep] [--impl ours|reference]
 
 Workloads:
+  muon8b  configs[4], the default at every N: FusedMuon.step() over the 224
+          matrices of the 8B-class Llama shape set, grads N(0, 1e-3), lr 0.02,
+          momentum 0.95, nesterov, matrices sharded across the N ranks
+          (FLOP-balanced) with an NCCL all-gather.  The same workload at
+          N = 1, 2, 4, 8 makes one strong-scaling curve.  At N = 1 the line
+          also carries, under "ns_4096", the configs[1] headline below.
+  muon1b  configs[3]: the same over the 112 matrices of the 1B-class set.
   ns      configs[1] headline: 5-step Newton-Schulz on one (4096, 4096) bf16
-          N(0,1) matrix (seed 0).  One step = one fused_newton_schulz call.
-          Default at N = 1.  L2 (126 MB) is flushed with a 256 MB write before
-          every timed step (outside the step's events).
-  muon1b  configs[3]: FusedMuon.step() over the 112 matrices of the 1B-class
-          Llama shape set, grads N(0, 1e-3), lr 0.02, momentum 0.95, nesterov.
-  muon8b  configs[4]: the same over the 224 matrices of the 8B-class set,
-          matrices sharded across the N ranks (FLOP-balanced) with an NCCL
-          all-gather of the bf16 updates.  Default at N > 1.
+          N(0,1) matrix (seed 0); --shape picks another (m, n).  One step =
+          one fused_newton_schulz call.  L2 (126 MB) is flushed with a 256 MB
+          write before every timed step (outside the step's events).
+  sweep   configs[0..2]: every NS shape of the config-1 case and the square
+          and wide sweeps, timed with the reference's own protocol
+          (benchmarks/bench_ns_step.py:41-81: 200 warm-ups, 50 timed calls,
+          median), beside the reference's PyTorch NS on the same GPU, eager
+          and under torch.compile.  One JSON line per shape.
 
 The metric is dense-equivalent Newton-Schulz TFLOP/s (the reference's count,
 5·(4m²n + 2m³) per matrix; docs/optimization_report.md:24-29), whole job, max
@@ -203,25 +210,28 @@ def torch_eager_ns(G: torch.Tensor, steps: int) -> torch.Tensor:
 
 
 # --------------------------------------------------------------------------- CPU arms
-def cpu_ns_sample(budget_s: float):
-    """Time the reference's algorithm (oracle restatement) on host cores on the
-    headline matrix; returns (TFLOP/s, seconds per call, calls, threads)."""
+def cpu_ns_sample(budget_s: float, shapes):
+    """Time the reference's algorithm (oracle restatement) on the host cores
+    over ``shapes`` (one seeded bf16 matrix each, one pass = every matrix
+    once); returns (TFLOP/s, seconds per pass, passes, threads)."""
     from oracle import ns_oracle as O
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    G = torch.randn(*SHAPE_NS, generator=torch.Generator().manual_seed(0)).bfloat16()
-    O.ns_reference_bf16(G[:512, :512], NS_STEPS)  # warm the BLAS
+    gs = [torch.randn(*s, generator=torch.Generator().manual_seed(i)).bfloat16()
+          for i, s in enumerate(shapes)]
+    O.ns_reference_bf16(gs[0][:512, :512], NS_STEPS)  # warm the BLAS
     times = []
     t_end = time.perf_counter() + budget_s
     while True:
         t0 = time.perf_counter()
-        O.ns_reference_bf16(G, NS_STEPS)
+        for g in gs:
+            O.ns_reference_bf16(g, NS_STEPS)
         times.append(time.perf_counter() - t0)
         if time.perf_counter() > t_end or len(times) >= 5:
             break
     med = statistics.median(times)
-    return ns_flops(*SHAPE_NS) / med / 1e12, med, len(times), threads
+    return sum(ns_flops(*sh) for sh in shapes) / med / 1e12, med, len(times), threads
 
 
 def run_reference_arm(args, world, rank):
@@ -233,8 +243,9 @@ def run_reference_arm(args, world, rank):
     torch.set_num_threads(threads)
     wl = args.workload
     if wl == "ns":
-        G = torch.randn(*SHAPE_NS, generator=torch.Generator().manual_seed(0)).bfloat16()
-        unit_flops, sample = ns_flops(*SHAPE_NS), "one 5-step NS on (4096,4096) per step"
+        m, n = args.shape
+        G = torch.randn(m, n, generator=torch.Generator().manual_seed(0)).bfloat16()
+        unit_flops, sample = ns_flops(m, n), f"one 5-step NS on ({m},{n}) per step"
         fn = lambda: O.ns_reference_bf16(G, NS_STEPS)
     else:
         # one layer of the set (7 matrices) per step; the metric is a rate, so
@@ -245,8 +256,12 @@ def run_reference_arm(args, world, rank):
         unit_flops = sum(ns_flops(*s) for s in shapes)
         sample = f"one layer ({len(shapes)} matrices) of the {wl} set per step, NS only"
         fn = lambda: [O.ns_reference_bf16(g, NS_STEPS) for g in gs]
+    # warm-up: W passes, but at most ~20 s of CPU work (at least one pass)
+    t_w = time.perf_counter()
     for _ in range(args.warmup):
         fn()
+        if time.perf_counter() - t_w > 20.0:
+            break
     # bounded sample: stop timing after ~60 s of CPU work (at least one step)
     times = []
     t_start = time.perf_counter()
@@ -259,13 +274,13 @@ def run_reference_arm(args, world, rank):
     t = statistics.mean(times)
     value = unit_flops / t / 1e12
     line = {
-        "impl": "reference", "metric": metric_name(wl), "value": round(value, 4),
+        "impl": "reference", "metric": metric_name(wl, tuple(args.shape)), "value": round(value, 4),
         "unit": "TFLOP/s", "n_gpus": world, "steps": len(times), "warmup": args.warmup,
         "steps_requested": args.steps,
         "ms_per_step": round(t * 1e3, 3), "higher_is_better": True,
         "scaling": "weak" if wl == "ns" else "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic",
-        "config": config_for(wl, world),
+        "config": config_for(wl, world, tuple(args.shape)),
         "cpu_baseline": {"value": round(value, 4), "unit": "TFLOP/s", "cores": threads,
                          "kind": "port", "sample": sample},
         "e2e": {"value": round(value, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
@@ -274,9 +289,9 @@ def run_reference_arm(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
-def metric_name(wl: str) -> str:
+def metric_name(wl: str, shape=SHAPE_NS) -> str:
     if wl == "ns":
-        return "5-step Newton-Schulz dense-equivalent TFLOP/s, (4096,4096) bf16"
+        return f"5-step Newton-Schulz dense-equivalent TFLOP/s, ({shape[0]},{shape[1]}) bf16"
     return f"FusedMuon.step Newton-Schulz dense-equivalent TFLOP/s, {wl} shape set"
 
 
@@ -331,8 +346,9 @@ def bench_ns(args, peaks, peak_src):
         fused_newton_schulz(G, NS_STEPS, ws)
     st = _lib.stage_times()
     _lib.stage_timing(False)
-    stage_flops = {"gemm1_syrk": 2.0 * m * m * n, "gemm2_poly": 2.0 * m ** 3,
-                   "gemm3_bx": 2.0 * m * m * n}
+    mo, no = min(m, n), max(m, n)  # the kernels work on the wide orientation
+    stage_flops = {"gemm1_syrk": 2.0 * mo * mo * no, "gemm2_poly": 2.0 * mo ** 3,
+                   "gemm3_bx": 2.0 * mo * mo * no}
     stages = {}
     for k, (tot, cnt) in st.items():
         if cnt:
@@ -346,14 +362,16 @@ def bench_ns(args, peaks, peak_src):
     avg_dom = st[dom][0] / st[dom][1]
     achieved = stage_flops[dom] / (avg_dom * 1e-3) / 1e12
     peak = float(peaks["bf16_tflops"])
-    roofline = {"bound": "tensor", "kernel": ("ns_gemm_pair_kernel<kBX>" if min(m, n) > 256 else "ns_gemm_kernel<kBX>") + " (X' = d*X + Boff*X)",
+    roofline = {"bound": "tensor",
+                "kernel": ("ns_gemm_pair_kernel<kBX>" if mo > 256 else "ns_gemm_kernel<kBX>")
+                + " (X' = d*X + Boff*X)",
                 "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
                 "frac": round(achieved / peak, 4), "peak_source": f"{peak_src} bf16_tflops (burst)",
                 "traffic": None, "stages": stages}
 
     extra = {"us_per_ns": round(ms * 1e3, 1),
-             "useful_tflops": round(NS_STEPS * (m * (m + 1) * n + m * m * (m + 1)
-                                                + 2.0 * m * m * n) / (ms * 1e-3) / 1e12, 1)}
+             "useful_tflops": round(NS_STEPS * (mo * (mo + 1) * no + mo * mo * (mo + 1)
+                                                + 2.0 * mo * mo * no) / (ms * 1e-3) / 1e12, 1)}
     if args.quick:
         return {"ms": ms, "flops": flops, "t_ms": t_ms, "roofline": roofline,
                 "clocks": clk.summary(), "e2e": None, "launches": launches,
@@ -524,8 +542,143 @@ def bench_muon(args, world, rank, peaks, peak_src):
            "d2h_bytes_per_step": probe.nbytes, "steps": e2e_steps,
            "mode": "pipelined: owned gradients uploaded from pinned host memory on a copy "
                    "stream during the previous step; rank 0's bytes"}
+    extra = {"matrices": len(shapes)}
+    if world > 1:
+        extra["ranks_agree"], extra["owner_check"] = verify_sharded(opt, params, shapes, owner,
+                                                                    world, rank)
     return {"ms": ms, "flops": flops, "roofline": roofline, "clocks": clk.summary(), "e2e": e2e,
-            "launches": launches, "extra": {"matrices": len(shapes)}}
+            "launches": launches, "extra": extra}
+
+
+def verify_sharded(opt, params, shapes, owner, world, rank):
+    """Correctness of the sharded step, after the timed loops (outside them).
+
+    1. Every rank holds bit-identical parameters: a float64 sum per matrix,
+       all-reduced with MAX and MIN, must agree exactly.
+    2. One more sharded step is replayed on rank 0 for three large matrices
+       owned by different ranks: their owners broadcast the momentum buffer,
+       rank 0 recomputes momentum (the reference's torch ops), a single-matrix
+       fused_newton_schulz and the update, and compares with the parameters
+       the sharded step produced (bit-identical expected: at these sizes the
+       batched and single calls run the same unsplit tiles; the line reports
+       the relative Frobenius difference of the deltas too)."""
+    import torch.distributed as dist
+
+    from muon_fused import fused_newton_schulz
+
+    sums = torch.stack([p.detach().double().sum() for p in params])
+    hi, lo = sums.clone(), sums.clone()
+    dist.all_reduce(hi, op=dist.ReduceOp.MAX)
+    dist.all_reduce(lo, op=dist.ReduceOp.MIN)
+    same = bool(torch.equal(hi, lo))
+
+    picked, ranks_seen = [], set()
+    for i, s in enumerate(shapes):
+        if min(s) >= 3072 and owner[i] not in ranks_seen:
+            picked.append(i)
+            ranks_seen.add(owner[i])
+        if len(picked) == 3:
+            break
+    before, bufs = {}, {}
+    for i in picked:
+        p = params[i]
+        buf = opt.state[p]["momentum_buffer"] if owner[i] == rank else torch.empty_like(p.grad)
+        dist.broadcast(buf, src=owner[i])
+        bufs[i] = buf.clone()
+        before[i] = p.detach().clone()
+    opt.step()
+    torch.cuda.synchronize()
+    group = opt.param_groups[0]
+    lr, wd, mu = group["lr"], group["wd"], group["momentum"]
+    worst, exact = 0.0, True
+    if rank == 0:
+        for i in picked:
+            g = params[i].grad
+            buf = bufs[i].mul_(mu).add_(g)
+            d = g.add(buf, alpha=mu)
+            u = fused_newton_schulz(d, NS_STEPS)
+            want = before[i].clone()
+            want.mul_(1 - lr * wd).add_(u, alpha=-opt.adjust_lr_for_muon(lr, want.shape))
+            got = params[i].detach()
+            exact = exact and bool(torch.equal(got, want))
+            dg = got.double() - before[i].double()
+            dw = want.double() - before[i].double()
+            worst = max(worst, float((dg - dw).norm() / dw.norm()))
+    flag = torch.tensor([1.0 if (same and worst <= 5e-3) else 0.0], device="cuda")
+    dist.broadcast(flag, src=0)
+    check = {"matrices": [list(shapes[i]) for i in picked], "owners": [owner[i] for i in picked],
+             "bit_identical": exact, "max_rel_fro_delta": worst, "checksums_equal": same}
+    return bool(flag.item() == 1.0), check
+
+
+SWEEP_SHAPES = [(896, 1152),  # configs[0]
+                (2048, 2048), (3584, 3584), (4096, 4096), (8192, 8192),  # configs[1]
+                (2048, 2560), (2560, 6144), (2560, 9728), (3584, 4608), (4096, 14336),
+                (4096, 28672)]  # configs[2]
+
+
+def bench_sweep(args, peaks, peak_src):
+    """Every NS shape of configs[0..2] with the reference's protocol
+    (benchmarks/bench_ns_step.py:62-81: warm-ups, then CUDA-event-timed calls,
+    median): ours, the reference's PyTorch NS eager, and the same under
+    torch.compile (the reference's published comparison compiles
+    zeropower_via_newtonschulz5, benchmarks/reference_muon.py:13-37).
+    Inputs are seeded N(0,1) bf16 resident on the GPU; no L2 flush (the
+    reference's harness has none)."""
+    from muon_fused import fused_newton_schulz, workspace_size
+
+    dev = torch.device("cuda")
+    compiled = torch.compile(torch_eager_ns)
+    peak = float(peaks["bf16_tflops"])
+    warm, timed = args.sweep_warmup, args.sweep_timed
+
+    def median_ms(fn, G, n_warm):
+        for _ in range(n_warm):
+            fn(G)
+        torch.cuda.synchronize()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(timed)]
+        for s_, e_ in evs:
+            s_.record()
+            fn(G)
+            e_.record()
+        torch.cuda.synchronize()
+        return statistics.median(s_.elapsed_time(e_) for s_, e_ in evs)
+
+    lines = []
+    for m, n in (args.sweep_shapes or SWEEP_SHAPES):
+        G = torch.randn(m, n, generator=torch.Generator(device=dev).manual_seed(0), device=dev,
+                        dtype=torch.bfloat16)
+        ws = torch.empty(workspace_size(m, n), dtype=torch.uint8, device=dev)
+        with ClockSampler(torch.cuda.current_device()) as clk:
+            ours = median_ms(lambda x: fused_newton_schulz(x, NS_STEPS, ws), G, warm)
+        eager = median_ms(lambda x: torch_eager_ns(x, NS_STEPS), G, 10)
+        try:
+            comp = median_ms(lambda x: compiled(x, NS_STEPS), G, 10)
+        except Exception as e:  # noqa: BLE001 - reported, not fatal
+            comp = None
+            comp_err = repr(e)[:200]
+        mo, no = min(m, n), max(m, n)
+        dense = ns_flops(m, n)
+        useful = NS_STEPS * (mo * (mo + 1) * no + mo * mo * (mo + 1) + 2.0 * mo * mo * no)
+        line = {"workload": "ns_sweep", "shape": [m, n], "us_per_ns": round(ours * 1e3, 1),
+                "dense_eq_tflops": round(dense / (ours * 1e-3) / 1e12, 1),
+                "useful_tflops": round(useful / (ours * 1e-3) / 1e12, 1),
+                "frac_of_measured_peak": round(dense / (ours * 1e-3) / 1e12 / peak, 4),
+                "peak": f"{peak} TFLOP/s ({peak_src} bf16_tflops, burst)",
+                "torch_eager_us": round(eager * 1e3, 1),
+                "torch_compile_us": None if comp is None else round(comp * 1e3, 1),
+                "speedup_vs_eager": round(eager / ours, 3),
+                "speedup_vs_compile": None if comp is None else round(comp / ours, 3),
+                "protocol": f"{warm} warm-ups, median of {timed} CUDA-event-timed calls",
+                "clocks": clk.summary()}
+        if comp is None:
+            line["torch_compile_error"] = comp_err
+        print(json.dumps(line), flush=True)
+        lines.append(line)
+        del G, ws
+        torch.cuda.empty_cache()
+    return lines
 
 
 def main():
@@ -535,24 +688,32 @@ def main():
                     help="timed steps (default: 400 for ns, 40 for the optimizer-step workloads, "
                          "so the timed work stays within about a minute)")
     ap.add_argument("--warmup", type=int, default=20)
-    ap.add_argument("--workload", choices=["ns", "muon1b", "muon8b"], default=None)
+    ap.add_argument("--workload", choices=["ns", "muon1b", "muon8b", "sweep"], default="muon8b")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--collective", choices=["nccl", "peer"], default="nccl",
-                    help="sharded-step exchange: NCCL all-gather + apply, or the fused "
-                         "peer-memory gather + apply kernel")
+    ap.add_argument("--collective", choices=["nccl", "param_gather"], default="param_gather",
+                    help="sharded-step exchange: all-gather of the updates + apply on every "
+                         "rank, or owner apply + in-place all-gather of the parameters")
     ap.add_argument("--shape", type=int, nargs=2, default=list(SHAPE_NS),
                     help="ns workload matrix shape (default: the headline 4096 4096)")
     ap.add_argument("--quick", action="store_true",
                     help="ns workload: timed loop and per-kernel pass only (for ncu launch lists)")
-    ap.add_argument("--cpu-budget", type=float, default=15.0,
-                    help="seconds of host-CPU baseline sampling (rank 0, N=1)")
+    ap.add_argument("--no-ns-headline", action="store_true",
+                    help="optimizer-step workloads at N = 1: skip the ns_4096 sub-object")
+    ap.add_argument("--cpu-budget", type=float, default=12.0,
+                    help="seconds of host-CPU baseline sampling per baseline (rank 0, N=1)")
+    ap.add_argument("--sweep-warmup", type=int, default=200)
+    ap.add_argument("--sweep-timed", type=int, default=50)
+    ap.add_argument("--sweep-shapes", type=int, nargs="+", default=None,
+                    help="sweep: flat list of m n pairs (default: all BASELINE shapes)")
     args = ap.parse_args()
+    if args.sweep_shapes:
+        v = args.sweep_shapes
+        args.sweep_shapes = [(v[i], v[i + 1]) for i in range(0, len(v) - 1, 2)]
     world, rank, local = dist_env()
-    if args.workload is None:
-        args.workload = "ns" if world == 1 else "muon8b"
     if args.steps is None:
         args.steps = 400 if args.workload == "ns" else 40
     args.warmup = max(args.warmup, 3)
+    args.shape = tuple(args.shape)
 
     if args.impl == "reference":
         run_reference_arm(args, world, rank)
@@ -564,23 +725,36 @@ def main():
 
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
     peaks, peak_src = load_peaks()
+    if args.workload == "sweep":
+        if rank == 0:
+            bench_sweep(args, peaks, peak_src)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+            dist.destroy_process_group()
+        return
+    ns_sub = None
     if args.workload == "ns":
-        args.shape = tuple(args.shape)
         r = bench_ns(args, peaks, peak_src)
         r["ms"] = barrier_max(r["ms"], world)
         value = world * r["flops"] / (r["ms"] * 1e-3) / 1e12
     else:
         r = bench_muon(args, world, rank, peaks, peak_src)
         value = r["flops"] / (r["ms"] * 1e-3) / 1e12
+        if world == 1 and not args.no_ns_headline:
+            torch.cuda.empty_cache()
+            ns_sub = ns_headline(args, peaks, peak_src)
 
     if rank == 0:
         line = {
-            "metric": metric_name(args.workload), "value": round(value, 2), "unit": "TFLOP/s",
+            "metric": metric_name(args.workload, args.shape), "value": round(value, 2),
+            "unit": "TFLOP/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(r["ms"], 4), "higher_is_better": True,
             "scaling": "weak" if args.workload == "ns" else "strong",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": dict(config_for(args.workload, world, getattr(args, "shape", SHAPE_NS)),
+            "config": dict(config_for(args.workload, world, args.shape),
                            **({"exchange": args.collective}
                               if world > 1 and args.workload != "ns" else {})),
             "clocks": r["clocks"], "gpu_launches": r["launches"],
@@ -590,17 +764,47 @@ def main():
         if r["roofline"] is not None:
             line["roofline"] = r["roofline"]
         line.update(r["extra"])
-        if world == 1 and args.workload == "ns" and not args.quick:
-            v, sec, calls, threads = cpu_ns_sample(args.cpu_budget)
+        if world == 1 and not args.quick:
+            if args.workload == "ns":
+                shapes, what = [args.shape], f"5-step NS on ({args.shape[0]},{args.shape[1]})"
+            else:
+                shapes = llama_shapes(args.workload)[:7]
+                what = f"5-step NS of one layer (7 matrices) of the {args.workload} set"
+            v, sec, calls, threads = cpu_ns_sample(args.cpu_budget, shapes)
             line["cpu_baseline"] = {"value": round(v, 4), "unit": "TFLOP/s", "cores": threads,
                                     "kind": "port",
-                                    "sample": f"{calls} x 5-step NS on (4096,4096), median {sec:.2f} s"}
+                                    "sample": f"{calls} x {what}, median {sec:.2f} s"}
+        if ns_sub is not None:
+            line["ns_4096"] = ns_sub
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
 
         dist.barrier()
         dist.destroy_process_group()
+
+
+def ns_headline(args, peaks, peak_src):
+    """configs[1] headline inside the N = 1 line: the (4096, 4096) 5-step NS
+    with its own device-timed rate, GEMM3 roofline, end-to-end rate from
+    pinned host memory, the reference's PyTorch path on this GPU and the host
+    CPU baseline of the same matrix."""
+    import argparse as _ap
+
+    a = _ap.Namespace(**vars(args))
+    a.shape, a.steps, a.warmup, a.quick = SHAPE_NS, 100, 20, False
+    r = bench_ns(a, peaks, peak_src)
+    v, sec, calls, threads = cpu_ns_sample(args.cpu_budget, [SHAPE_NS])
+    out = {"metric": metric_name("ns", SHAPE_NS), "unit": "TFLOP/s",
+           "value": round(r["flops"] / (r["ms"] * 1e-3) / 1e12, 2),
+           "ms_per_step": round(r["ms"], 4), "steps": a.steps, "warmup": a.warmup,
+           "config": config_for("ns", 1, SHAPE_NS), "clocks": r["clocks"], "e2e": r["e2e"],
+           "roofline": r["roofline"],
+           "cpu_baseline": {"value": round(v, 4), "unit": "TFLOP/s", "cores": threads,
+                            "kind": "port",
+                            "sample": f"{calls} x 5-step NS on (4096,4096), median {sec:.2f} s"}}
+    out.update(r["extra"])
+    return out
 
 
 if __name__ == "__main__":

@@ -169,45 +169,6 @@ int fm_muon_apply(void* param, int dtype, const void* update, int64_t n, float d
                   void* stream);
 
 /*
- * Peer-memory gather + update for the sharded optimizer step (one process
- * per GPU, CUDA IPC over NVLink; no multicast).
- *
- * fm_peer_alloc: cudaMalloc `bytes` (zeroed) and export its 64-byte IPC
- *   handle; fm_peer_open maps a peer's handle, fm_peer_close unmaps,
- *   fm_peer_free releases an fm_peer_alloc buffer.
- * fm_peer_signal: after all prior work on `stream`, store `value` to the
- *   64-bit flag with release semantics at system scope.
- * fm_peer_gather_apply: for each of `nentries` parameters (entries in device
- *   memory), wait (bounded, about 10 s) until flag
- *   peer_flags[entry.peer][flag_index] >= expected, then apply
- *   p = round(round(p * entry.decay) + entry.alpha * u) with the bf16 update
- *   u = peer_src[entry.peer] + src_shift + entry.src_offset read directly
- *   from the owner's memory.  `peer_src` and `peer_flags` are device arrays
- *   of one pointer per rank.  A wait that runs out sets code 5 in the device
- *   error word (fm_device_error) and skips that parameter.
- * Replaces: the NCCL all-gather + local apply of the sharded step (which
- *   itself replaces the reference's unsharded loop, optimizer.py:128-163).
- */
-typedef struct fm_apply_entry {
-  void* param;         /* parameter data (dtype below), numel elements */
-  int64_t numel;
-  int64_t src_offset;  /* element offset of this update in its owner's send buffer */
-  float decay;         /* 1 - lr * wd */
-  float alpha;         /* -lr * 0.2 * sqrt(max(A, B)) */
-  int32_t dtype;       /* FM_DT_F32 / FM_DT_BF16 / FM_DT_F16 */
-  int32_t peer;        /* owner rank */
-} fm_apply_entry;
-
-int fm_peer_alloc(uint64_t bytes, void** ptr, void* ipc_handle);
-int fm_peer_open(const void* ipc_handle, void** ptr);
-int fm_peer_close(void* ptr);
-int fm_peer_free(void* ptr);
-int fm_peer_signal(int64_t* flag, int64_t value, void* stream);
-int fm_peer_gather_apply(const fm_apply_entry* entries, int nentries, const void* const* peer_src,
-                         int64_t src_shift, const int64_t* const* peer_flags, int flag_index,
-                         int64_t expected, void* stream);
-
-/*
  * GEMM kernel selection for all later calls in the process:
  * 0 = automatic (CTA-pair 256x256 tiles for matrices with more than 256
  * rows after orientation, single-CTA 128x256 tiles otherwise),

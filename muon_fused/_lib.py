@@ -38,12 +38,6 @@ SIGNATURES = {
     "fm_fused_newton_schulz_noalloc": (_c_int, [_vp, _c_int, _i64, _i64, _i64, _vp, _c_int, _vp]),
     "fm_muon_momentum": (_c_int, [_vp, _vp, _vp, _i64, _c_int, ctypes.c_float, _c_int, _vp]),
     "fm_muon_apply": (_c_int, [_vp, _c_int, _vp, _i64, ctypes.c_float, ctypes.c_float, _vp]),
-    "fm_peer_alloc": (_c_int, [_u64, ctypes.POINTER(_vp), _vp]),
-    "fm_peer_open": (_c_int, [_vp, ctypes.POINTER(_vp)]),
-    "fm_peer_close": (_c_int, [_vp]),
-    "fm_peer_free": (_c_int, [_vp]),
-    "fm_peer_signal": (_c_int, [_vp, _i64, _vp]),
-    "fm_peer_gather_apply": (_c_int, [_vp, _c_int, _vp, _i64, _vp, _c_int, _i64, _vp]),
     "fm_set_gemm_path": (_c_int, [_c_int]),
     "fm_stage_timing": (_c_int, [_c_int]),
     "fm_stage_times": (_c_int, [ctypes.POINTER(ctypes.c_float), ctypes.POINTER(_c_int)]),

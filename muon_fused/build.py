@@ -19,7 +19,7 @@ CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libfused_muon.so")
 SOURCES = ["ns_capi.cu"]
 DEPS = SOURCES + ["fm_ptx.cuh", "ns_gemm_sm100.cuh", "ns_gemm2_sm100.cuh", "ns_prep.cuh",
-                  "muon_elementwise.cuh", "peer_apply.cuh"]
+                  "muon_elementwise.cuh"]
 HEADER = os.path.join(os.path.dirname(HERE), "include", "fused_muon.h")
 
 NVCC_FLAGS = [

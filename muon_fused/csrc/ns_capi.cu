@@ -23,7 +23,6 @@
 #include "ns_gemm_sm100.cuh"
 #include "muon_elementwise.cuh"
 #include "ns_prep.cuh"
-#include "peer_apply.cuh"
 
 namespace fm {
 
@@ -51,8 +50,10 @@ int fail(int code, const char* fmt, ...) {
 
 constexpr int kMaxDevices = 64;
 
+// `ready` is published with release semantics after every other field is
+// written, and read with acquire semantics on the lock-free fast path.
 struct DeviceState {
-  bool ready = false;
+  std::atomic<bool> ready{false};
   int sm_count = 0;
   unsigned* err_word = nullptr;
 };
@@ -109,9 +110,9 @@ int device_state(DeviceState** out) {
   FM_CUDA(cudaGetDevice(&dev));
   if (dev < 0 || dev >= kMaxDevices) return fail(FM_E_DEVICE, "device index %d out of range", dev);
   DeviceState& s = g_dev[dev];
-  if (!s.ready) {
+  if (!s.ready.load(std::memory_order_acquire)) {
     std::lock_guard<std::mutex> lk(g_mu);
-    if (!s.ready) {
+    if (!s.ready.load(std::memory_order_relaxed)) {
       int major = 0, minor = 0;
       FM_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev));
       FM_CUDA(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev));
@@ -131,11 +132,6 @@ int device_state(DeviceState** out) {
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, kPairSmemBytes));
       FM_CUDA(cudaFuncSetAttribute(ns_gemm_pair_kernel<kBX>,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, kPairSmemBytes));
-      // The peer apply kernel runs beside the GEMMs on a side stream: with the
-      // default (small) shared-memory carveout an SM hosting it could not take
-      // a GEMM CTA until it drained, so it asks for the GEMMs' configuration.
-      FM_CUDA(cudaFuncSetAttribute(peer_gather_apply_kernel,
-                                   cudaFuncAttributePreferredSharedMemoryCarveout, 100));
       FM_CUDA(cudaGetSymbolAddress(reinterpret_cast<void**>(&s.err_word), g_device_error));
       if (!g_encode) {
         cudaDriverEntryPointQueryResult q;
@@ -145,7 +141,7 @@ int device_state(DeviceState** out) {
           return fail(FM_E_CUDA, "cuTensorMapEncodeTiled entry point not found");
         g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
       }
-      s.ready = true;
+      s.ready.store(true, std::memory_order_release);
     }
   }
   *out = &s;
@@ -671,63 +667,6 @@ int fm_muon_apply(void* param, int dtype, const void* update, int64_t n, float d
   return FM_OK;
 }
 
-int fm_peer_alloc(uint64_t bytes, void** ptr, void* ipc_handle) {
-  if (!ptr || !ipc_handle || bytes == 0) return fail(FM_E_INVALID, "bad fm_peer_alloc arguments");
-  void* p = nullptr;
-  FM_CUDA(cudaMalloc(&p, bytes));
-  cudaError_t e = cudaMemset(p, 0, bytes);
-  if (e == cudaSuccess) e = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(ipc_handle), p);
-  if (e != cudaSuccess) {
-    cudaFree(p);
-    return fail(FM_E_CUDA, "fm_peer_alloc: %s", cudaGetErrorString(e));
-  }
-  *ptr = p;
-  return FM_OK;
-}
-
-int fm_peer_open(const void* ipc_handle, void** ptr) {
-  if (!ptr || !ipc_handle) return fail(FM_E_INVALID, "null pointer argument");
-  cudaIpcMemHandle_t h;
-  std::memcpy(&h, ipc_handle, sizeof(h));
-  FM_CUDA(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess));
-  return FM_OK;
-}
-
-int fm_peer_close(void* ptr) {
-  FM_CUDA(cudaIpcCloseMemHandle(ptr));
-  return FM_OK;
-}
-
-int fm_peer_free(void* ptr) {
-  FM_CUDA(cudaFree(ptr));
-  return FM_OK;
-}
-
-int fm_peer_signal(int64_t* flag, int64_t value, void* stream) {
-  if (!flag) return fail(FM_E_INVALID, "null flag");
-  peer_signal_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(
-      reinterpret_cast<long long*>(flag), static_cast<long long>(value));
-  FM_CUDA(cudaGetLastError());
-  note_launch();
-  return FM_OK;
-}
-
-int fm_peer_gather_apply(const fm_apply_entry* entries, int nentries, const void* const* peer_src,
-                         int64_t src_shift, const int64_t* const* peer_flags, int flag_index,
-                         int64_t expected, void* stream) {
-  if (nentries <= 0) return FM_OK;
-  if (!entries || !peer_src || !peer_flags) return fail(FM_E_INVALID, "null pointer argument");
-  DeviceState* ds;
-  if (int rc = device_state(&ds)) return rc;
-  peer_gather_apply_kernel<<<ds->sm_count, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      entries, nentries, reinterpret_cast<const __nv_bfloat16* const*>(peer_src), src_shift,
-      reinterpret_cast<const long long* const*>(peer_flags), flag_index,
-      static_cast<long long>(expected), ds->err_word);
-  FM_CUDA(cudaGetLastError());
-  note_launch();
-  return FM_OK;
-}
-
 int fm_set_gemm_path(int path) {
   if (path < 0 || path > 2) return fail(FM_E_INVALID, "gemm path must be 0, 1 or 2, got %d", path);
   g_gemm_path.store(path);
@@ -778,23 +717,24 @@ int fm_stage_times(float* ms, int* counts) {
 static __device__ __align__(256) unsigned char g_static_scratch[FM_STATIC_SCRATCH_BYTES];
 
 namespace {
-void* g_static_scratch_ptr[kMaxDevices];
+std::atomic<void*> g_static_scratch_ptr[kMaxDevices];
 std::mutex g_static_mu;
 
 int static_scratch(void** out) {
   int dev = 0;
   FM_CUDA(cudaGetDevice(&dev));
   if (dev < 0 || dev >= kMaxDevices) return fail(FM_E_DEVICE, "device index %d out of range", dev);
-  if (!g_static_scratch_ptr[dev]) {
+  void* cached = g_static_scratch_ptr[dev].load(std::memory_order_acquire);
+  if (!cached) {
     std::lock_guard<std::mutex> lk(g_static_mu);
-    if (!g_static_scratch_ptr[dev]) {
-      void* p = nullptr;
-      FM_CUDA(cudaGetSymbolAddress(&p, g_static_scratch));
-      if (!p) return fail(FM_E_CUDA, "cudaGetSymbolAddress returned a null scratch address");
-      g_static_scratch_ptr[dev] = p;
+    cached = g_static_scratch_ptr[dev].load(std::memory_order_relaxed);
+    if (!cached) {
+      FM_CUDA(cudaGetSymbolAddress(&cached, g_static_scratch));
+      if (!cached) return fail(FM_E_CUDA, "cudaGetSymbolAddress returned a null scratch address");
+      g_static_scratch_ptr[dev].store(cached, std::memory_order_release);
     }
   }
-  *out = g_static_scratch_ptr[dev];
+  *out = cached;
   return FM_OK;
 }
 }  // namespace

@@ -65,9 +65,12 @@ class FusedMuon(Optimizer):
             its inputs, outputs and workspace (default 4 GiB); same-shape
             matrices are batched up to this budget.
         collective: how a sharded step shares the updates: ``"nccl"`` (bucketed
-            NCCL all-gather, then a local apply) or ``"peer"`` (a fused kernel
-            reads each owner's send buffer over NVLink via CUDA IPC and
-            applies the update in the same pass).
+            all-gather of the bf16 updates, then every rank applies every
+            update) or ``"param_gather"`` (each owner applies its own updates,
+            then the bucket's parameters are all-gathered in place; the
+            parameters' ``.data`` are moved into per-bucket flat buffers for
+            this, see ``sharding.ParamStore``).  Both give bit-identical
+            parameters.
     """
 
     def __init__(
@@ -96,10 +99,10 @@ class FusedMuon(Optimizer):
         self._batch_bytes = int(batch_bytes)
         self._plans: dict[tuple, Any] = {}
         self._arena: dict[torch.device, torch.Tensor] = {}
-        if collective not in ("nccl", "peer"):
-            raise ValueError(f"collective must be 'nccl' or 'peer', got {collective!r}")
+        if collective not in ("nccl", "param_gather"):
+            raise ValueError(f"collective must be 'nccl' or 'param_gather', got {collective!r}")
         self._collective = collective
-        self._exchanges: dict[tuple, Any] = {}
+        self._stores: dict[tuple, Any] = {}
         # id(group) -> (params, owner rank per param, momentum dtype per param)
         # of the group's last sharded step (consolidate_state_dict)
         self._owners: dict[int, tuple] = {}
@@ -263,27 +266,15 @@ class FusedMuon(Optimizer):
             self._apply_update(params[i], u, group["lr"], group["wd"])
 
         dev = params[0].device
-        if self._collective == "peer" and self._peer_ok(params, pg):
-            ex = self._exchanges.get(key)
-            if ex is None:
-                ex = sharding.PeerExchange(plan, rank, pg, dev)
-                self._exchanges[key] = ex
-            lr, wd = group["lr"], group["wd"]
-            decay_alpha = [(float(1 - lr * wd), float(-self.adjust_lr_for_muon(lr, p.shape)))
-                           for p in params]
-            sharding.run_sharded_peer(ex, params, decay_alpha, compute)
+        if self._collective == "param_gather" and sharding.ParamStore.supports(params):
+            store = self._stores.get(key)
+            if store is None:
+                store = sharding.ParamStore(plan, params, dev)
+                self._stores[key] = store
+            store.bind(params)
+            sharding.run_sharded_param_gather(store, rank, pg, compute, apply)
             return
         sharding.run_sharded(plan, rank, pg, dev, compute, apply)
-
-    @staticmethod
-    def _peer_ok(params, pg) -> bool:
-        """The peer-memory exchange needs NCCL-backed CUDA ranks and contiguous
-        parameters of a dtype the fused update handles."""
-        import torch.distributed as dist
-
-        if dist.get_backend(pg) != "nccl":
-            return False
-        return all(p.is_cuda and p.data.is_contiguous() and p.dtype in _EW_DTYPES for p in params)
 
     # ------------------------------------------------------------------ AdamW
     def _adamw_group(self, group) -> None:

@@ -13,7 +13,10 @@ matrix's update is independent, so here:
    ``all_gather`` on gloo) as soon as it is packed, so the transfer of bucket
    k overlaps the Newton-Schulz work of bucket k+1;
 4. every rank then applies the decay + update to every parameter from the
-   gathered buffers.
+   gathered buffers (``collective="nccl"``), or — ``collective="param_gather"``
+   — each owner applies its own updates in place and the bucket's parameters
+   themselves are all-gathered in place into every rank's parameter storage
+   (``ParamStore``), so non-owners do no apply pass at all.
 
 Gradients must already be identical on all ranks (data parallel after the
 gradient all-reduce), which is what makes the owner's update the update.
@@ -129,20 +132,10 @@ def run_sharded(plan: ShardPlan, rank: int, pg, device, compute, apply) -> None:
             continue
         send = torch.empty(size, dtype=torch.bfloat16, device=device)
         mine = row[rank]
-        j = 0
-        while j < len(mine):
-            # a run of consecutive same-shape matrices is one batched call
-            i0, off0 = mine[j]
-            shape = plan.shapes[i0]
-            e = j + 1
-            while e < len(mine) and plan.shapes[mine[e][0]] == shape:
-                e += 1
+        for idx, off0, n, shape in _runs(plan, mine):
             rows = shape[0]
             cols = numel(shape) // rows
-            n = e - j
-            out = send[off0:off0 + n * rows * cols].view(n, rows, cols)
-            compute([i for i, _ in mine[j:e]], out)
-            j = e
+            compute(idx, send[off0:off0 + n * rows * cols].view(n, rows, cols))
         used = max((off + numel(plan.shapes[i]) for i, off in mine[-1:]), default=0)
         if used < size:
             send[used:].zero_()  # padding up to the largest rank's share
@@ -169,186 +162,114 @@ def _apply_bucket(plan: ShardPlan, item, apply) -> None:
 
 
 # --------------------------------------------------------------------------
-# Peer-memory exchange: all-gather and apply fused into one kernel that reads
-# each owner's send buffer over NVLink (fm_peer_gather_apply).
-class _DevicePtr:
-    """Zero-copy view of a library-owned device buffer (CUDA array interface)."""
+# Owner apply + in-place parameter gather (collective="param_gather").
+class ParamStore:
+    """Per-bucket flat parameter storage laid out like the all-gather output.
 
-    def __init__(self, ptr: int, nbytes: int):
-        self.__cuda_array_interface__ = {"shape": (nbytes // 2,), "typestr": "<i2",
-                                         "data": (ptr, False), "version": 3, "strides": None}
+    Bucket k holds ``world`` chunks of ``plan.bucket_numel[k]`` elements; rank
+    r's chunk packs, at the plan's offsets, the parameters r owns in bucket
+    k.  Every parameter's ``.data`` is re-pointed to a view of its slot (the
+    current values are copied in first), so the Parameter objects the caller
+    holds stay the same while their storage moves.  Then a step needs no
+    receive buffer and no apply pass on non-owners: each owner updates its
+    own parameters in place and one in-place all-gather per bucket delivers
+    the new values straight into every rank's parameter storage.
 
-
-_ENTRY_DTYPE = None
-
-
-def _entry_dtype():
-    """numpy layout of fm_apply_entry (include/fused_muon.h)."""
-    global _ENTRY_DTYPE
-    if _ENTRY_DTYPE is None:
-        import numpy as np
-
-        _ENTRY_DTYPE = np.dtype([("param", "<u8"), ("numel", "<i8"), ("src_offset", "<i8"),
-                                 ("decay", "<f4"), ("alpha", "<f4"), ("dtype", "<i4"),
-                                 ("peer", "<i4")])
-        assert _ENTRY_DTYPE.itemsize == 40
-    return _ENTRY_DTYPE
-
-
-class PeerExchange:
-    """Double-buffered send buffers and per-bucket flags shared over CUDA IPC.
-
-    Rank r owns a send buffer of 2 x share bf16 elements (step parity) and a
-    flag array of 2 x buckets int64.  Every rank maps every other rank's
-    buffers once (``all_gather_object`` of the IPC handles), so a step needs
-    no collective call at all: owners raise ``flag[bucket] = step`` after the
-    bucket's Newton-Schulz, readers wait on it inside the apply kernel.
+    If a caller later replaces ``p.data`` (so the pointer leaves the slot),
+    ``bind`` copies the new value back into the slot before the step.
     """
 
-    def __init__(self, plan: ShardPlan, rank: int, pg, device):
-        import ctypes
+    def __init__(self, plan: ShardPlan, params, device):
+        self.plan = plan
+        self.dtype = params[0].dtype
+        self.flats = [torch.zeros(plan.world * size, dtype=self.dtype, device=device)
+                      for size in plan.bucket_numel]
+        self.slots: list = [None] * len(params)
+        for k, row in enumerate(plan.buckets):
+            size = plan.bucket_numel[k]
+            for r in range(plan.world):
+                for i, off in row[r]:
+                    base = r * size + off
+                    self.slots[i] = self.flats[k][base:base + numel(plan.shapes[i])].view(
+                        plan.shapes[i])
+        self.bind(params)
 
-        import torch.distributed as dist
+    @staticmethod
+    def supports(params) -> bool:
+        """One dtype, one device, contiguous, and no parameter sharing storage
+        with another (re-pointing would split a tied weight)."""
+        if not params:
+            return False
+        dt, dev = params[0].dtype, params[0].device
+        seen = set()
+        for p in params:
+            if p.dtype != dt or p.device != dev or not p.data.is_contiguous():
+                return False
+            key = p.data.untyped_storage().data_ptr()
+            if key in seen:
+                return False
+            seen.add(key)
+        return True
 
-        from muon_fused import _lib
-
-        lib = _lib.load()
-        self.plan, self.rank, self.world = plan, rank, plan.world
-        self.device = device
-        self.nb = len(plan.buckets)
-        self.bucket_off = []
-        off = 0
-        for k in range(self.nb):
-            self.bucket_off.append(off)
-            off += plan.bucket_numel[k]
-        self.share = max(off, 1)
-        self._own = []
-        handles = []
-        with torch.cuda.device(device):
-            for nbytes in (2 * self.share * 2, 2 * self.nb * 8):
-                ptr = ctypes.c_void_p()
-                h = ctypes.create_string_buffer(64)
-                _lib.check(lib.fm_peer_alloc(nbytes, ctypes.byref(ptr), h), "fm_peer_alloc")
-                self._own.append(ptr.value)
-                handles.append(h.raw)
-        gathered = [None] * self.world
-        dist.all_gather_object(gathered, handles, group=pg)
-        self._opened = []
-        src, flags = [], []
-        with torch.cuda.device(device):
-            for r in range(self.world):
-                if r == rank:
-                    src.append(self._own[0])
-                    flags.append(self._own[1])
-                    continue
-                ptrs = []
-                for h in gathered[r]:
-                    p = ctypes.c_void_p()
-                    _lib.check(lib.fm_peer_open(ctypes.create_string_buffer(h, 64), ctypes.byref(p)),
-                               "fm_peer_open")
-                    ptrs.append(p.value)
-                    self._opened.append(p.value)
-                src.append(ptrs[0])
-                flags.append(ptrs[1])
-        self.peer_src = torch.tensor(src, dtype=torch.int64, device=device)
-        self.peer_flags = torch.tensor(flags, dtype=torch.int64, device=device)
-        self.send = torch.as_tensor(_DevicePtr(self._own[0], 2 * self.share * 2),
-                                    device=device).view(torch.bfloat16)
-        self.step = 0
-        self._tables = None
-        self._table_key = None
-
-    def side_stream(self):
-        if getattr(self, "_side", None) is None:
-            self._side = torch.cuda.Stream(device=self.device)
-        return self._side
-
-    def bucket_view(self, k: int, parity: int) -> torch.Tensor:
-        base = parity * self.share + self.bucket_off[k]
-        return self.send[base:base + self.plan.bucket_numel[k]]
-
-    def tables(self, params, decay_alpha):
-        """Per-bucket device tables of fm_apply_entry, rebuilt when lr/wd change."""
-        import numpy as np
-
-        from muon_fused.optimizer import _EW_DTYPES
-
-        key = (tuple(decay_alpha), tuple(p.data_ptr() for p in params))
-        if self._table_key == key:
-            return self._tables
-        out = []
-        for k, row in enumerate(self.plan.buckets):
-            items = [(r, i, off) for r in range(self.world) for i, off in row[r]]
-            arr = np.zeros(len(items), dtype=_entry_dtype())
-            for j, (r, i, off) in enumerate(items):
-                p = params[i].data
-                arr[j] = (p.data_ptr(), p.numel(), self.bucket_off[k] + off, decay_alpha[i][0],
-                          decay_alpha[i][1], _EW_DTYPES[p.dtype], r)
-            t = torch.from_numpy(arr.view(np.uint8)).to(self.device)
-            out.append((t, len(items)))
-        self._tables, self._table_key = out, key
-        return out
-
-    def close(self):
-        from muon_fused import _lib
-
-        lib = _lib.load()
-        for p in self._opened:
-            lib.fm_peer_close(p)
-        for p in self._own:
-            lib.fm_peer_free(p)
-        self._opened, self._own = [], []
+    def bind(self, params) -> None:
+        for p, slot in zip(params, self.slots):
+            if p.data.data_ptr() != slot.data_ptr():
+                slot.copy_(p.data)
+                p.data = slot
 
 
-def run_sharded_peer(ex: PeerExchange, params, decay_alpha, compute) -> None:
-    """One sharded step over peer memory.  ``compute(indices, out)`` as in
-    run_sharded.  Updates are applied by fm_peer_gather_apply on a side
-    stream: bucket k's kernel (started once this rank's bucket k is done)
-    waits on the GPU for every owner's flag of bucket k and reads over NVLink
-    while later buckets are computed on the current stream.  The side stream first waits for the current stream (the
-    parameters may still be read by earlier work) and the current stream
-    waits for it at the end."""
-    from muon_fused import _lib
+def _all_gather_inplace(flat: torch.Tensor, rank: int, pg, world: int):
+    """All-gather whose input is this rank's own chunk of the output."""
+    import torch.distributed as dist
 
-    lib = _lib.load()
-    plan, rank = ex.plan, ex.rank
-    ex.step += 1
-    parity = ex.step % 2
-    cur = torch.cuda.current_stream(ex.device)
-    stream = cur.cuda_stream
-    side = ex.side_stream()
-    side.wait_stream(cur)
-    tables = ex.tables(params, decay_alpha)
+    chunks = flat.chunk(world)
+    if dist.get_backend(pg) == "nccl":
+        return dist.all_gather_into_tensor(flat, chunks[rank], group=pg, async_op=True)
+    return dist.all_gather(list(chunks), chunks[rank].clone(), group=pg, async_op=True)
 
-    def apply(k):
-        t, n = tables[k]
-        _lib.check(lib.fm_peer_gather_apply(
-            t.data_ptr(), n, ex.peer_src.data_ptr(), parity * ex.share, ex.peer_flags.data_ptr(),
-            parity * ex.nb + k, ex.step, side.cuda_stream), "fm_peer_gather_apply")
 
+def run_sharded_param_gather(store: ParamStore, rank: int, pg, compute, apply) -> None:
+    """One sharded step with owner-side apply.
+
+    For each bucket: ``compute(indices, out)`` writes the owned matrices'
+    bf16 updates into a scratch buffer, ``apply(i, u)`` updates parameter i
+    in place (it lives in this rank's chunk of the bucket's flat storage),
+    then the bucket is all-gathered in place, asynchronously, so its
+    transfer overlaps the next bucket's Newton-Schulz.  At the end the
+    current stream waits for every gather, so later kernels on it (the next
+    forward pass) read the new parameters.
+    """
+    plan = store.plan
+    world = plan.world
+    dev = store.flats[0].device if store.flats else None
+    cap = max((plan.bucket_numel[k] for k in range(len(plan.buckets))), default=0)
+    upd = torch.empty(max(cap, 1), dtype=torch.bfloat16, device=dev)
+    works = []
     for k, row in enumerate(plan.buckets):
-        send = ex.bucket_view(k, parity)
+        if plan.bucket_numel[k] == 0:
+            continue
         mine = row[rank]
-        j = 0
-        while j < len(mine):
-            i0, off0 = mine[j]
-            shape = plan.shapes[i0]
-            e = j + 1
-            while e < len(mine) and plan.shapes[mine[e][0]] == shape:
-                e += 1
+        for idx, off0, n, shape in _runs(plan, mine):
             rows = shape[0]
             cols = numel(shape) // rows
-            out = send[off0:off0 + (e - j) * rows * cols].view(e - j, rows, cols)
-            compute([i for i, _ in mine[j:e]], out)
-            j = e
-        _lib.check(lib.fm_peer_signal(ex._own[1] + 8 * (parity * ex.nb + k), ex.step, stream),
-                   "fm_peer_signal")
-        # The apply of bucket k starts only after this rank's own bucket k is
-        # done and signalled: then every rank raises flag k before any of its
-        # apply blocks can sit on SMs waiting for others, so the waits cannot
-        # form a cycle even where the blocks keep GEMM CTAs waiting.
-        done = torch.cuda.Event()
-        done.record(cur)
-        side.wait_event(done)
-        apply(k)
-    cur.wait_stream(side)
+            out = upd[off0:off0 + n * rows * cols].view(n, rows, cols)
+            compute(idx, out)
+            for j, i in enumerate(idx):
+                apply(i, out[j])
+        works.append(_all_gather_inplace(store.flats[k], rank, pg, world))
+    for w in works:
+        w.wait()
+
+
+def _runs(plan: ShardPlan, mine):
+    """Consecutive same-shape matrices of one rank's bucket share: one batched
+    Newton-Schulz call each.  Yields (indices, offset, count, shape)."""
+    j = 0
+    while j < len(mine):
+        i0, off0 = mine[j]
+        shape = plan.shapes[i0]
+        e = j + 1
+        while e < len(mine) and plan.shapes[mine[e][0]] == shape:
+            e += 1
+        yield [i for i, _ in mine[j:e]], off0, e - j, shape
+        j = e

@@ -1,7 +1,7 @@
 """Generate the golden vectors in this folder from the reference itself.
 
-Runs only where the reference checkout exists (default ``/root/reference``,
-override with ``FUSED_MUON_REFERENCE``); the committed ``ns_golden.pt`` is what
+Runs only where a reference checkout exists: pass its path as the first
+argument or in ``FUSED_MUON_REFERENCE``; the committed ``ns_golden.pt`` is what
 the tests read, so nothing at test time needs the reference.
 
 What is recorded (all on CPU, the reference's pure-PyTorch path):
@@ -16,7 +16,7 @@ What is recorded (all on CPU, the reference's pure-PyTorch path):
   the ``@torch.compile`` wrapper cannot build on a CPU-only box) on a small
   parameter set with ``use_muon`` and AdamW groups.
 
-Usage: python tests/golden/make_golden.py
+Usage: python tests/golden/make_golden.py <path to the reference checkout>
 """
 
 from __future__ import annotations
@@ -28,7 +28,7 @@ import sys
 
 import torch
 
-REF = os.environ.get("FUSED_MUON_REFERENCE", "/root/reference")
+REF = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("FUSED_MUON_REFERENCE", "")
 OUT = os.path.join(os.path.dirname(os.path.abspath(__file__)), "ns_golden.pt")
 
 NS_CASES = [
@@ -82,6 +82,9 @@ MUON_STEPS = 3
 
 
 def main() -> None:
+    if not REF or not os.path.isdir(REF):
+        sys.exit("usage: make_golden.py <path to the reference checkout> "
+                 "(or set FUSED_MUON_REFERENCE)")
     torch.set_num_threads(1)
     sys.path.insert(0, REF)
     ns = _load("ref_ns_step", os.path.join(REF, "muon_fused", "ns_step.py"))

@@ -85,3 +85,45 @@ def test_split_k_single_matrix(cuda_lib, shape):
     if shape[0] * shape[1] <= 1 << 21:
         assert O.rel_fro(a.cpu(), O.ns_fp32(G, 5)) <= 1e-2
     assert _lib.device_error() == 0
+
+
+def _set_shapes():
+    """Distinct Muon matrix shapes of the 1B and 8B sets (BASELINE configs 4
+    and 5) with their counts: q/o, k/v, gate/up, down per layer."""
+    out = []
+    for h, kv, ffn, layers in ((2048, 512, 8192, 16), (4096, 1024, 14336, 32)):
+        out += [((h, h), 2 * layers), ((kv, h), 2 * layers), ((ffn, h), 2 * layers),
+                ((h, ffn), layers)]
+    return out
+
+
+@pytest.mark.parametrize("shape,count", _set_shapes(),
+                         ids=[f"{s[0]}x{s[1]}" for s, _ in _set_shapes()])
+def test_optimizer_batches_full_size(cuda_lib, shape, count):
+    """One batched call per distinct 1B/8B shape at the batch size FusedMuon
+    forms for it (FusedMuon._batch_limit under the default 4 GiB budget,
+    capped by the matrices of that shape in the set), tall gate/up shapes
+    included.  A sample of each batch (first, middle, last matrix) is gated
+    against the fp32 restatement on the GPU with TF32 off, <= 1e-2."""
+    from muon_fused import FusedMuon
+    from muon_fused import _fused_muon_C as _C
+
+    rows, cols = shape
+    opt = FusedMuon([torch.nn.Parameter(torch.zeros(1, device=DEV))])
+    b = min(count, opt._batch_limit(rows, cols))
+    gen = torch.Generator(device=DEV).manual_seed(rows * 7 + cols)
+    G = (torch.randn(b, rows, cols, generator=gen, device=DEV) * 1e-3).bfloat16()
+    out = _C.fused_newton_schulz_batched(G, 5)
+    torch.cuda.synchronize()
+    assert out.shape == G.shape
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        for i in sorted({0, b // 2, b - 1}):
+            ref = O.ns_fp32(G[i], 5)
+            assert O.rel_fro(out[i], ref) <= 1e-2, (shape, b, i)
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    from muon_fused import _lib
+
+    assert _lib.device_error() == 0

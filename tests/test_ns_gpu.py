@@ -247,3 +247,31 @@ def test_normalisation_bit_exact(cuda_lib, batch, rows, cols, kmax):
         den = torch.sqrt(torch.tensor(s, dtype=torch.float32)) + 1e-7
         ref = (G[b].float() / den).to(torch.bfloat16)
         assert torch.equal(out[b], ref), b
+
+
+@pytest.mark.parametrize("m,n", [(256, 384), (384, 448), (200, 440), (3072, 3072), (3072, 4096)])
+def test_single_cta_and_pair_kernels_bit_identical(cuda_lib, m, n):
+    """The single-CTA (128x256 tiles) and CTA-pair (256x256 tiles) kernels
+    run the same per-element arithmetic: every output element is one fp32
+    accumulation over K in the same K-block order, then the same epilogue.
+    Where neither path splits K, one iteration gives bit-identical A, Boff,
+    diag and X'.  The pair path splits K only when a GEMM has fewer than 74
+    tiles and at least 8 K-blocks, so the shapes here have either K <= 448
+    (short reductions) or m >= 3072 (78+ lower-triangle pair tiles).  With a
+    K-split the fp32 partial sums are added in a different order and agree
+    only to rounding (test_split_k_single_matrix)."""
+    from muon_fused import _fused_muon_C as _C
+    from muon_fused import _lib
+
+    X = torch.randn(m, n, generator=torch.Generator().manual_seed(m + n)).bfloat16().to(DEV)
+    X = (X.float() / X.float().norm()).bfloat16()
+    res = {}
+    try:
+        for path in (1, 2):
+            _lib.set_gemm_path(path)
+            res[path] = _C.ns_step_debug(X)
+    finally:
+        _lib.set_gemm_path(0)
+    torch.cuda.synchronize()
+    for a, b, name in zip(res[1], res[2], ("A", "Boff", "diag", "X_new")):
+        assert torch.equal(a, b), name

@@ -185,3 +185,54 @@ def test_fused_elementwise_bit_identical_to_torch_ops(cuda_lib, dtype, nesterov)
                                       stream), "apply")
     torch.cuda.synchronize()
     assert torch.equal(p, ref_p)
+
+
+def test_full_1b_set_step_matches_fp32_ns_trajectory(cuda_lib):
+    """BASELINE config 4 at full size: one FusedMuon.step() over all 112
+    matrices of the 1B-class set (bf16 N(0, 1e-3) gradients, lr 0.02,
+    momentum 0.95, nesterov, 5 NS steps), so every batch FusedMuon forms for
+    this set runs.  A sample (every shape, first and last layer) is checked
+    against the oracle's step with the fp32 Newton-Schulz, run on the GPU
+    with TF32 off: the parameter deltas agree to 1e-2 and the momentum
+    buffers are bit-identical.  Parameters are fp32 here so that the delta
+    is not quantised by bf16 parameter rounding (an ulp of a 0.02-sized bf16
+    value is ~3% of an update); the bf16-parameter path is covered by the
+    bit-identity tests of the apply kernel."""
+    from muon_fused import FusedMuon
+
+    h, kv, ffn, layers = 2048, 512, 8192, 16
+    per_layer = [(h, h), (kv, h), (kv, h), (h, h), (ffn, h), (ffn, h), (h, ffn)]
+    shapes = [s for _ in range(layers) for s in per_layer]
+    params, grads = [], []
+    for i, s in enumerate(shapes):
+        g = torch.Generator(device=DEV).manual_seed(i)
+        params.append(torch.nn.Parameter(
+            torch.randn(s, generator=g, device=DEV) * 0.02))
+        g = torch.Generator(device=DEV).manual_seed(1000 + i)
+        grads.append((torch.randn(s, generator=g, device=DEV) * 1e-3).bfloat16())
+    sample = [0, 1, 4, 6, len(shapes) - 7 + 3, len(shapes) - 7 + 5, len(shapes) - 1]
+    init = {i: params[i].detach().clone() for i in sample}
+    for p, g in zip(params, grads):
+        p.grad = g
+    opt = FusedMuon([{"params": params, "use_muon": True}], lr=0.02, momentum=0.95,
+                    nesterov=True, ns_steps=5)
+    opt.step()
+    torch.cuda.synchronize()
+    ref = [torch.nn.Parameter(init[i].clone()) for i in sample]
+    for p, i in zip(ref, sample):
+        p.grad = grads[i]
+    state = {}
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        O.muon_reference_step([dict(params=ref, use_muon=True, lr=0.02, wd=0.1, momentum=0.95,
+                                    nesterov=True, ns_steps=5)], state, ns=O.ns_fp32)
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    torch.cuda.synchronize()
+    for p, i in zip(ref, sample):
+        got = params[i].detach() - init[i]
+        want = p.detach() - init[i]
+        assert O.rel_fro(got, want) <= 1e-2, (i, shapes[i])
+        assert torch.equal(opt.state[params[i]]["momentum_buffer"],
+                           state[id(p)]["momentum_buffer"]), i

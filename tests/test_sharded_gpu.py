@@ -69,23 +69,23 @@ def _worker(rank, world, port, outdir, collective):
 
 
 def test_sharded_nccl_matches_single_gpu(cuda_lib):
-    """Both exchanges (NCCL all-gather; fused peer-memory gather + apply over
-    NVLink) give every rank the same parameters, bit-identical between the
-    two exchanges, and equal to the single-GPU run up to summation order.
-    Three steps exercise both parities of the peer send buffers.  After
+    """Both exchanges (NCCL all-gather of the updates + apply on every rank;
+    owner apply + in-place NCCL all-gather of the parameters) give every rank
+    the same parameters, bit-identical between the two exchanges, and equal
+    to the single-GPU run up to summation order.  After
     consolidate_state_dict() every rank holds every momentum buffer, equal to
     the single-GPU run's."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     ref, ref_mom = _run(_params(torch.device("cuda", 0)), torch.device("cuda", 0))
     outdir = tempfile.mkdtemp()
-    for collective in ("nccl", "peer"):
+    for collective in ("nccl", "param_gather"):
         mp.spawn(_worker, args=(2, _port(), outdir, collective), nprocs=2, join=True)
     from oracle import ns_oracle as O
 
     init = [p.detach().cpu() for p in _params("cpu")]
     got = {c: [torch.load(os.path.join(outdir, f"{c}{r}.pt")) for r in range(2)]
-           for c in ("nccl", "peer")}
+           for c in ("nccl", "param_gather")}
     for c in got:
         for a, b in zip(got[c][0][0], got[c][1][0]):
             assert torch.equal(a, b)  # every rank applied the same updates
@@ -94,7 +94,7 @@ def test_sharded_nccl_matches_single_gpu(cuda_lib):
             for a, b in zip(got[c][r][1], ref_mom):
                 assert torch.equal(a, b)
     got = {c: [v[0] for v in got[c]] for c in got}
-    for a, b in zip(got["nccl"][0], got["peer"][0]):
+    for a, b in zip(got["nccl"][0], got["param_gather"][0]):
         assert torch.equal(a, b)  # same arithmetic, different transport
     # Batches differ between the sharded and the single-GPU run (so may the
     # K-splits): equal up to fp32 summation order inside the GEMMs.

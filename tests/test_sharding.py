@@ -55,10 +55,11 @@ def _patch_ns():
     om._ns_batched = ns_batched_cpu
 
 
-def _run_steps(params, steps, bucket_bytes):
+def _run_steps(params, steps, bucket_bytes, collective="nccl"):
     from muon_fused import FusedMuon
 
-    opt = FusedMuon([{"params": params, "use_muon": True}], lr=0.02, bucket_bytes=bucket_bytes)
+    opt = FusedMuon([{"params": params, "use_muon": True}], lr=0.02, bucket_bytes=bucket_bytes,
+                    collective=collective)
     for s in range(steps):
         for p, g in zip(params, _grads(s)):
             p.grad = g.clone()
@@ -66,7 +67,7 @@ def _run_steps(params, steps, bucket_bytes):
     return opt
 
 
-def _worker(rank, world, port, outdir, bucket_bytes, leave_rank):
+def _worker(rank, world, port, outdir, bucket_bytes, leave_rank, collective="nccl"):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     import datetime
@@ -80,9 +81,11 @@ def _worker(rank, world, port, outdir, bucket_bytes, leave_rank):
             # leaves between steps: no collective of this rank is in flight
             dist.destroy_process_group()
             return
-        opt = _run_steps(params, 2, bucket_bytes)
+        ids = [id(p) for p in params]
+        opt = _run_steps(params, 2, bucket_bytes, collective)
+        assert [id(p) for p in opt.param_groups[0]["params"]] == ids  # same Parameter objects
         owned = sorted(i for i, p in enumerate(params) if "momentum_buffer" in opt.state[p])
-        torch.save({"params": [p.detach() for p in params], "owned": owned},
+        torch.save({"params": [p.detach().clone() for p in params], "owned": owned},
                    os.path.join(outdir, f"rank{rank}.pt"))
     except Exception as e:  # recorded for the parent to inspect
         with open(os.path.join(outdir, f"rank{rank}.err"), "w") as f:
@@ -95,10 +98,10 @@ def _worker(rank, world, port, outdir, bucket_bytes, leave_rank):
                 pass
 
 
-def _spawn(world, bucket_bytes=1 << 30, leave_rank=None):
+def _spawn(world, bucket_bytes=1 << 30, leave_rank=None, collective="nccl"):
     outdir = tempfile.mkdtemp()
-    mp.spawn(_worker, args=(world, _free_port(), outdir, bucket_bytes, leave_rank), nprocs=world,
-             join=True)
+    mp.spawn(_worker, args=(world, _free_port(), outdir, bucket_bytes, leave_rank, collective),
+             nprocs=world, join=True)
     return outdir
 
 
@@ -147,10 +150,14 @@ def test_plan_8b_shapes_balance():
         assert max(loads) / (total / world) < 1.03
 
 
-@pytest.mark.parametrize("world", [2, 4])
-def test_sharded_equals_single_process(world):
+@pytest.mark.parametrize("world,collective", [(2, "nccl"), (4, "nccl"), (2, "param_gather"),
+                                               (4, "param_gather")])
+def test_sharded_equals_single_process(world, collective):
+    """Both exchanges: the update all-gather + apply everywhere, and the
+    owner apply + in-place parameter all-gather (non-owners apply nothing)."""
     ref = _single_process()
-    outdir = _spawn(world, bucket_bytes=8192)  # small buckets: several all-gathers
+    # small buckets: several all-gathers
+    outdir = _spawn(world, bucket_bytes=8192, collective=collective)
     results = [torch.load(os.path.join(outdir, f"rank{r}.pt")) for r in range(world)]
     owned = []
     for r, res in enumerate(results):
@@ -166,6 +173,25 @@ def test_rank_leaving_between_steps_is_an_error():
     assert not os.path.exists(os.path.join(outdir, "rank0.pt"))
     with open(os.path.join(outdir, "rank0.err")) as f:
         assert f.read()
+
+
+def test_param_store_repoints_and_rebinds():
+    """ParamStore moves each parameter into its bucket slot (same Parameter
+    object, same values) and copies a replaced ``.data`` back into the slot."""
+    from muon_fused.sharding import ParamStore
+
+    params = _make()
+    before = [p.detach().clone() for p in params]
+    plan = ShardPlan.build([tuple(p.shape) for p in params], 3, bucket_bytes=4096)
+    store = ParamStore(plan, params, torch.device("cpu"))
+    for p, b, slot in zip(params, before, store.slots):
+        assert p.data_ptr() == slot.data_ptr() and torch.equal(p.detach(), b)
+    params[2].data = torch.full_like(params[2].data, 7.0)
+    store.bind(params)
+    assert params[2].data_ptr() == store.slots[2].data_ptr()
+    assert torch.all(store.slots[2] == 7.0)
+    # tied weights (shared storage) are not supported: the plain exchange is used
+    assert not ParamStore.supports([params[0], params[0]])
 
 
 def _ckpt_worker(rank, world, port, outdir):

@@ -6,9 +6,12 @@ cudaMalloc could stall or fail.  For them the library offers a Newton-Schulz
 call whose scratch lives in a fixed device array inside the library.  This
 test calls it through the C ABI, twice in a row on different inputs (the
 array keeps the previous call's contents), and checks each result against the
-regular entry point with a caller-allocated workspace, within the 1e-2
-relative-Frobenius tolerance the other parity tests use.  It also checks that
-an oversized matrix is refused with a clear error.
+regular entry point with a caller-allocated workspace.  Both run the same
+plan and the same arithmetic, so the gate is bit equality (tighter than the
+1e-2 relative-Frobenius tolerance against fp32 that the other parity tests
+use, which is checked too).  It also checks that a call leaves the device's
+free memory unchanged (the library allocates nothing behind torch's back) and
+that an oversized matrix is refused with a clear error.
 
 The file name sorts last so that a run stopping at the first failure has run
 every other test already; it passes alone and after the others.
@@ -37,10 +40,11 @@ def _regular(lib, G, steps):
     return out
 
 
-def _noalloc(lib, G, steps):
+def _noalloc(lib, G, steps, out=None):
     from muon_fused import _lib
 
-    out = torch.empty(G.shape, dtype=torch.bfloat16, device=DEV)
+    if out is None:
+        out = torch.empty(G.shape, dtype=torch.bfloat16, device=DEV)
     rc = lib.fm_fused_newton_schulz_noalloc(G.data_ptr(), _lib.FM_DT_BF16, G.shape[0],
                                             G.shape[1], G.stride(0), out.data_ptr(), steps,
                                             torch.cuda.current_stream().cuda_stream)
@@ -59,9 +63,26 @@ def test_noalloc_matches_regular_entry_point(cuda_lib):
         want = _regular(cuda_lib, Gd, 5)
         torch.cuda.synchronize()
         assert got.shape == G.shape and got.dtype == torch.bfloat16
-        assert O.rel_fro(got, want) <= 1e-2, (rows, cols)
+        assert torch.equal(got, want), (rows, cols)
         assert O.rel_fro(got.cpu(), O.ns_fp32(G, 5)) <= 1e-2, (rows, cols)
     assert _lib.device_error() == 0
+
+
+def test_noalloc_allocates_no_device_memory(cuda_lib):
+    """After a warm-up call (which may load the module and look up the
+    array's address), a further call on a fresh input leaves the device's
+    free memory exactly as it was."""
+    G0 = torch.randn(1024, 2048, generator=torch.Generator().manual_seed(3)).bfloat16().to(DEV)
+    G1 = torch.randn(1024, 2048, generator=torch.Generator().manual_seed(4)).bfloat16().to(DEV)
+    out = torch.empty(G1.shape, dtype=torch.bfloat16, device=DEV)
+    _noalloc(cuda_lib, G0, 5)
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    _noalloc(cuda_lib, G1, 5, out=out)
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0
+    assert torch.equal(out, _regular(cuda_lib, G1, 5))
 
 
 def test_noalloc_rejects_oversized(cuda_lib):
