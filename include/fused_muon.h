@@ -170,10 +170,11 @@ int fm_muon_apply(void* param, int dtype, const void* update, int64_t n, float d
 
 /*
  * GEMM kernel selection for all later calls in the process:
- * 0 = automatic (CTA-pair 256x256 tiles for matrices with more than 256
- * rows after orientation, single-CTA 128x256 tiles otherwise),
- * 1 = always single-CTA, 2 = always CTA pairs.  Both produce the same
- * arithmetic; the switch exists for tests and tuning.
+ * 0 = automatic, 1 = one launch per GEMM with single-CTA 128x256 tiles,
+ * 2 = one launch per GEMM with CTA-pair 256x256 tiles, 3 = one persistent
+ * launch for all iterations with 128x256 tiles, 4 = the same with 128x128
+ * tiles.  All produce the same arithmetic (up to fp32 summation order where a
+ * path splits K); the switch exists for tests and tuning.
  * Replaces: the reference's compile-time tile dispatch, csrc/ns_gemm.cu:68-92.
  */
 int fm_set_gemm_path(int path);
@@ -184,7 +185,8 @@ int fm_set_gemm_path(int path);
  * (fm_stage_timing(0) stops it; either call discards pending pairs).
  * fm_stage_times() waits for the recorded events and returns, per stage, the
  * summed milliseconds and the launch count since the last read:
- * [0] GEMM1 A = X·Xᵀ, [1] GEMM2 polynomial, [2] GEMM3 X' = B·X, [3] norm/scale.
+ * [0] GEMM1 A = X·Xᵀ, [1] GEMM2 polynomial, [2] GEMM3 X' = B·X, [3] norm/scale,
+ * [4] the persistent kernel that runs all iterations in one launch.
  * Replaces: nothing; the reference has no instrumentation
  * (its timing lives in benchmarks/bench_ns_step.py:53-81).
  */

@@ -97,7 +97,7 @@ def device_error() -> int:
     return int(code.value)
 
 
-STAGES = ("gemm1_syrk", "gemm2_poly", "gemm3_bx", "prep")
+STAGES = ("gemm1_syrk", "gemm2_poly", "gemm3_bx", "prep", "fused_ns")
 
 
 def stage_timing(enable: bool) -> None:
@@ -106,10 +106,10 @@ def stage_timing(enable: bool) -> None:
 
 def stage_times():
     """{stage: (total ms, launches)} since the last read (see fm_stage_times)."""
-    ms = (ctypes.c_float * 4)()
-    cnt = (ctypes.c_int * 4)()
+    ms = (ctypes.c_float * len(STAGES))()
+    cnt = (ctypes.c_int * len(STAGES))()
     check(load().fm_stage_times(ms, cnt), "fm_stage_times")
-    return {STAGES[i]: (float(ms[i]), int(cnt[i])) for i in range(4)}
+    return {STAGES[i]: (float(ms[i]), int(cnt[i])) for i in range(len(STAGES))}
 
 
 def launch_count() -> int:
@@ -120,5 +120,6 @@ def launch_count() -> int:
 
 
 def set_gemm_path(path: int) -> None:
-    """0 automatic, 1 single-CTA tiles, 2 CTA-pair tiles (see fm_set_gemm_path)."""
+    """0 automatic, 1 single-CTA tiles, 2 CTA-pair tiles, 3/4 persistent kernel
+    with 128x256 / 128x128 tiles (see fm_set_gemm_path)."""
     check(load().fm_set_gemm_path(int(path)), "fm_set_gemm_path")

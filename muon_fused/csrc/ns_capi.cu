@@ -21,6 +21,7 @@
 #include "../../include/fused_muon.h"
 #include "ns_gemm2_sm100.cuh"
 #include "ns_gemm_sm100.cuh"
+#include "ns_fused_sm100.cuh"
 #include "muon_elementwise.cuh"
 #include "ns_prep.cuh"
 
@@ -66,7 +67,8 @@ inline long long round_up(long long x, long long a) { return (x + a - 1) / a * a
 // Optional per-stage timing for benchmarks (fm_stage_timing / fm_stage_times):
 // when enabled, each kernel launch of this thread is bracketed by CUDA events
 // on its stream; the pairs are resolved and summed per stage on request.
-constexpr int kStages4 = 4;  // 0 GEMM1 (X·Xᵀ), 1 GEMM2 (poly), 2 GEMM3 (B·X), 3 prep kernels
+// 0 GEMM1 (X·Xᵀ), 1 GEMM2 (poly), 2 GEMM3 (B·X), 3 prep kernels, 4 persistent NS kernel
+constexpr int kStages4 = 5;
 struct StageTimer {
   bool on = false;
   std::vector<cudaEvent_t> pool;
@@ -132,6 +134,12 @@ int device_state(DeviceState** out) {
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, kPairSmemBytes));
       FM_CUDA(cudaFuncSetAttribute(ns_gemm_pair_kernel<kBX>,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, kPairSmemBytes));
+      FM_CUDA(cudaFuncSetAttribute(ns_fused_kernel<256>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   FusedCfg<256>::kSmem));
+      FM_CUDA(cudaFuncSetAttribute(ns_fused_kernel<128>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   FusedCfg<128>::kSmem));
       FM_CUDA(cudaGetSymbolAddress(reinterpret_cast<void**>(&s.err_word), g_device_error));
       if (!g_encode) {
         cudaDriverEntryPointQueryResult q;
@@ -150,9 +158,11 @@ int device_state(DeviceState** out) {
 
 // 3-D bf16 tensor map over `batch` row-major rows x cols matrices with row
 // stride ld and matrix stride bstride (elements); box = box_cols (inner) x
-// box_rows x 1, 128-byte swizzle, zero fill out of bounds.
+// box_rows x 1, zero fill out of bounds.  Operand maps use the 128-byte
+// swizzle of the MMA's shared-memory layout; store maps none.
 int make_map(CUtensorMap* map, const void* base, long long batch, long long rows, long long cols,
-             long long ld, long long bstride, int box_cols, int box_rows) {
+             long long ld, long long bstride, int box_cols, int box_rows,
+             CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
   if (batch == 1) bstride = round_up(rows * ld, 8);
   if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (ld * 2) % 16 != 0 ||
       (bstride * 2) % 16 != 0)
@@ -163,16 +173,27 @@ int make_map(CUtensorMap* map, const void* base, long long batch, long long rows
   cuuint32_t box[3] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows), 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims,
-                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                        swz == CU_TENSOR_MAP_SWIZZLE_NONE ? CU_TENSOR_MAP_L2_PROMOTION_NONE
+                                                          : CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(FM_E_CUDA, "cuTensorMapEncodeTiled failed (%d)", int(r));
   return FM_OK;
 }
 
+// Epilogue store map (32 x 32 boxes) of a destination, or *ok = false when
+// its rows are not 16-byte aligned (the epilogue then stores directly).
+int make_store_map(CUtensorMap* map, bool* ok, const void* base, long long batch, long long rows,
+                   long long cols, long long ld, long long bstride) {
+  const long long bs = batch == 1 ? round_up(rows * ld, 8) : bstride;
+  *ok = (reinterpret_cast<uintptr_t>(base) & 15) == 0 && (ld * 2) % 16 == 0 && (bs * 2) % 16 == 0;
+  if (!*ok) return FM_OK;
+  return make_map(map, base, batch, rows, cols, ld, bstride, 32, 32, CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
 // GEMM kernel selection (fm_set_gemm_path): 0 = automatic, 1 = single-CTA
-// 128x256 tiles, 2 = CTA-pair 256x256 tiles.  Automatic uses CTA pairs for
-// batches and once the matrix spans more than one 256-row block.
+// 128x256 tiles, 2 = CTA-pair 256x256 tiles, 3 = persistent kernel over all
+// iterations with 128x256 tiles, 4 = the same with 128x128 tiles.
 std::atomic<int> g_gemm_path{0};
 
 // Kernels this library has launched in the process (fm_launch_count).
@@ -243,6 +264,7 @@ struct Workspace {
   float* partials;  // Frobenius-norm partials, kMaxPartials per matrix
   float* splitk;    // split-K fp32 partial tiles (128 KB per unit and CTA)
   int* counters;    // split-K arrival counters (two per tile: one per CTA)
+  int* phase;       // persistent kernel: phase-completion counters (kFusedSlots)
   long long ldx, ldm, xs, ms, dsz;  // row strides and per-matrix strides (elements)
   size_t counter_bytes;
   size_t bytes;
@@ -272,6 +294,7 @@ Workspace layout(long long batch, long long m, long long n, void* base) {
   w.partials = reinterpret_cast<float*>(p + off); off += pb;
   w.splitk = reinterpret_cast<float*>(p + off); off += sb;
   w.counters = reinterpret_cast<int*>(p + off); off += w.counter_bytes;
+  w.phase = reinterpret_cast<int*>(p + off); off += 256;
   w.bytes = off;
   return w;
 }
@@ -306,14 +329,14 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
 }
 
 template <int MODE>
-int launch_gemm(const DeviceState& ds, const CUtensorMap& ma, const CUtensorMap& mb, GemmArgs g,
-                cudaStream_t st) {
+int launch_gemm(const DeviceState& ds, const CUtensorMap& ma, const CUtensorMap& mb,
+                const CUtensorMap& mo, GemmArgs g, cudaStream_t st) {
   g.err = ds.err_word;
   if (g.num_tiles <= 0) return FM_OK;
   const int grid = std::min(g.num_tiles, ds.sm_count);
   const long long tm = timer_begin(MODE, st);
   FM_CUDA(launch_pdl(ns_gemm_kernel<MODE>, dim3(grid), dim3(kThreads), kSmemBytes, st, false, ma,
-                     mb, g));
+                     mb, mo, g));
   timer_end(tm, st);
   return FM_OK;
 }
@@ -322,13 +345,13 @@ int launch_gemm(const DeviceState& ds, const CUtensorMap& ma, const CUtensorMap&
 // two SMs, persistent over the work units.
 template <int MODE>
 int launch_gemm_pair(const DeviceState& ds, const CUtensorMap& ma, const CUtensorMap& mb,
-                     GemmArgs g, cudaStream_t st) {
+                     const CUtensorMap& mo, GemmArgs g, cudaStream_t st) {
   g.err = ds.err_word;
   if (g.num_tiles <= 0) return FM_OK;
   const int pairs = std::min(g.num_tiles, ds.sm_count / 2);
   const long long tm = timer_begin(MODE, st);
   FM_CUDA(launch_pdl(ns_gemm_pair_kernel<MODE>, dim3(2 * pairs), dim3(kThreads), kPairSmemBytes, st,
-                     true, ma, mb, g));
+                     true, ma, mb, mo, g));
   timer_end(tm, st);
   return FM_OK;
 }
@@ -344,15 +367,16 @@ struct IterIO {
 
 template <int MODE>
 int run_gemm(const DeviceState& ds, const NsPlan& P, const GemmPlan& gp, long long batch,
-             const CUtensorMap& ma, const CUtensorMap& mb, GemmArgs g, cudaStream_t st) {
+             const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mo, GemmArgs g,
+             cudaStream_t st) {
   g.batch = int(batch);
   g.tiles = gp.tiles;
   g.split = gp.split;
   g.kb_per_split = gp.kbps;
   g.num_tiles = int(batch * gp.tiles * gp.split);
-  if (P.pairs) return launch_gemm_pair<MODE>(ds, ma, mb, g, st);
+  if (P.pairs) return launch_gemm_pair<MODE>(ds, ma, mb, mo, g, st);
   g.num_tiles = gp.tiles;  // single-CTA kernel: batch == 1, split == 1
-  return launch_gemm<MODE>(ds, ma, mb, g, st);
+  return launch_gemm<MODE>(ds, ma, mb, mo, g, st);
 }
 
 int ns_iteration(const DeviceState& ds, const Workspace& w, const NsPlan& P, long long batch,
@@ -371,12 +395,19 @@ int ns_iteration(const DeviceState& ds, const Workspace& w, const NsPlan& P, lon
     }
     return FM_OK;
   }
-  CUtensorMap mx_k, mx_mn, ma, mbm;
+  CUtensorMap mx_k, mx_mn, ma, mbm, so_a, so_b, so_x;
   int rc;
   if ((rc = make_map(&mx_k, io.cur, batch, m, n, io.ldc, io.cur_bs, kBK, kBM))) return rc;
   if ((rc = make_map(&mx_mn, io.cur, batch, m, n, io.ldc, io.cur_bs, 64, kBK))) return rc;
   if ((rc = make_map(&ma, w.A, batch, m, m, w.ldm, w.ms, kBK, kBM))) return rc;
   if ((rc = make_map(&mbm, w.B, batch, m, m, w.ldm, w.ms, kBK, kBM))) return rc;
+  bool ok_a, ok_b, ok_x;
+  if ((rc = make_store_map(&so_a, &ok_a, w.A, batch, m, m, w.ldm, w.ms))) return rc;
+  if ((rc = make_store_map(&so_b, &ok_b, w.B, batch, m, m, w.ldm, w.ms))) return rc;
+  // X' (m x n), or X'ᵀ (n x m) when the last step writes a tall output
+  if ((rc = make_store_map(&so_x, &ok_x, io.nxt, batch, io.transpose_out ? n : m,
+                           io.transpose_out ? m : n, io.out_ld, io.out_bs)))
+    return rc;
 
   GemmArgs base{};
   base.M = int(m);
@@ -389,7 +420,8 @@ int ns_iteration(const DeviceState& ds, const Workspace& w, const NsPlan& P, lon
   GemmArgs g1 = base;
   g1.N = int(m); g1.K = int(n);
   g1.out = w.A; g1.ld_out = w.ldm; g1.bs_out = w.ms;
-  if ((rc = run_gemm<kSyrk>(ds, P, P.g[0], batch, mx_k, mx_k, g1, st))) return rc;
+  g1.tma_out = ok_a;
+  if ((rc = run_gemm<kSyrk>(ds, P, P.g[0], batch, mx_k, mx_k, ok_a ? so_a : ma, g1, st))) return rc;
 
   // GEMM2: Boff = offdiag(c·A·A + b·A), diag = a + diag(c·A·A + b·A)
   GemmArgs g2 = base;
@@ -397,7 +429,8 @@ int ns_iteration(const DeviceState& ds, const Workspace& w, const NsPlan& P, lon
   g2.out = w.B; g2.ld_out = w.ldm; g2.bs_out = w.ms;
   g2.aux = w.A; g2.ld_aux = w.ldm; g2.bs_aux = w.ms;
   g2.diag = w.diag; g2.bs_diag = w.dsz;
-  if ((rc = run_gemm<kPoly>(ds, P, P.g[1], batch, ma, ma, g2, st))) return rc;
+  g2.tma_out = ok_b;
+  if ((rc = run_gemm<kPoly>(ds, P, P.g[1], batch, ma, ma, ok_b ? so_b : ma, g2, st))) return rc;
 
   // GEMM3: X' = diag ⊙ X + Boff·X
   GemmArgs g3 = base;
@@ -406,7 +439,8 @@ int ns_iteration(const DeviceState& ds, const Workspace& w, const NsPlan& P, lon
   g3.transpose_out = io.transpose_out;
   g3.aux = io.cur; g3.ld_aux = io.ldc; g3.bs_aux = io.cur_bs;
   g3.diag = w.diag; g3.bs_diag = w.dsz;
-  return run_gemm<kBX>(ds, P, P.g[2], batch, mbm, mx_mn, g3, st);
+  g3.tma_out = ok_x;
+  return run_gemm<kBX>(ds, P, P.g[2], batch, mbm, mx_mn, ok_x ? so_x : ma, g3, st);
 }
 
 int check_dims(long long rows, long long cols) {
@@ -424,6 +458,95 @@ int prep_grid(long long rows, long long cols, const DeviceState& ds) {
   const long long want = (chunks + kPrepThreads * kFlatUnroll - 1) / (kPrepThreads * kFlatUnroll);
   const long long cap = std::min<long long>(kMaxPartials, ds.sm_count * 4ll);
   return int(std::max<long long>(1, std::min(want, cap)));
+}
+
+// All `steps` iterations of a batch in one persistent launch (ns_fused_sm100.cuh):
+// one CTA per SM, launched cooperatively so that every CTA is resident (the
+// phase-completion waits rely on it), with programmatic stream serialization
+// so its prologue overlaps the normalisation kernel.
+template <int BN>
+int run_fused(const DeviceState& ds, const Workspace& w, long long batch, long long m, long long n,
+              int steps, __nv_bfloat16* out, long long out_ld, long long out_bs, bool tall,
+              cudaStream_t st) {
+  FusedMaps maps;
+  int rc;
+  for (int i = 0; i < 2; ++i) {
+    if ((rc = make_map(&maps.xk[i], w.X[i], batch, m, n, w.ldx, w.xs, kBK, kBM))) return rc;
+    if ((rc = make_map(&maps.xmn[i], w.X[i], batch, m, n, w.ldx, w.xs, 64, kBK))) return rc;
+  }
+  if ((rc = make_map(&maps.a, w.A, batch, m, m, w.ldm, w.ms, kBK, kBM))) return rc;
+  if ((rc = make_map(&maps.b, w.B, batch, m, m, w.ldm, w.ms, kBK, kBM))) return rc;
+  bool ok;
+  if ((rc = make_store_map(&maps.so_a, &ok, w.A, batch, m, m, w.ldm, w.ms)) || !ok)
+    return rc ? rc : fail(FM_E_INVALID, "workspace A not TMA-addressable");
+  if ((rc = make_store_map(&maps.so_b, &ok, w.B, batch, m, m, w.ldm, w.ms)) || !ok)
+    return rc ? rc : fail(FM_E_INVALID, "workspace B not TMA-addressable");
+  for (int i = 0; i < 2; ++i)
+    if ((rc = make_store_map(&maps.so_x[i], &ok, w.X[i], batch, m, n, w.ldx, w.xs)) || !ok)
+      return rc ? rc : fail(FM_E_INVALID, "workspace X not TMA-addressable");
+  bool ok_out;
+  if ((rc = make_store_map(&maps.so_out, &ok_out, out, batch, tall ? n : m, tall ? m : n, out_ld,
+                           out_bs)))
+    return rc;
+  if (!ok_out) maps.so_out = maps.so_x[0];  // unused: the last step stores directly
+  FusedArgs f{};
+  f.M = int(m);
+  f.N = int(n);
+  f.batch = int(batch);
+  f.steps = steps;
+  f.t_syrk = fused_syrk_tiles<BN>(int(m));
+  f.tiles_m3 = int((m + kBM - 1) / kBM);
+  f.tiles_n3 = int((n + BN - 1) / BN);
+  const long long upi = batch * (2ll * f.t_syrk + static_cast<long long>(f.tiles_m3) * f.tiles_n3);
+  if (upi * steps > (1ll << 30)) return fail(FM_E_INVALID, "too many work units for one launch");
+  f.units_iter = int(upi);
+  f.X[0] = w.X[0];
+  f.X[1] = w.X[1];
+  f.ldx = w.ldx;
+  f.xs = w.xs;
+  f.A = w.A;
+  f.B = w.B;
+  f.ldm = w.ldm;
+  f.ms = w.ms;
+  f.diag = w.diag;
+  f.dsz = w.dsz;
+  f.out = out;
+  f.out_ld = out_ld;
+  f.out_bs = out_bs;
+  f.transpose_out = tall ? 1 : 0;
+  f.tma_out_final = ok_out ? 1 : 0;
+  f.counters = w.phase;  // zeroed by the caller before the normalisation kernels
+  f.err = ds.err_word;
+  const int grid = int(std::min<long long>(ds.sm_count, upi * steps));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = FusedCfg<BN>::kSmem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  const long long tm = timer_begin(4, st);
+  FM_CUDA(cudaLaunchKernelEx(&cfg, ns_fused_kernel<BN>, maps, f));
+  note_launch();
+  timer_end(tm, st);
+  return FM_OK;
+}
+
+// Automatic choice of the persistent kernel (128 x 128 tiles): when one wave
+// of SMs covers a whole SYRK phase, i.e. the batch's lower-triangle 128 x 128
+// tiles fit on the SMs.  Then every phase is latency-bound (one tile per SM)
+// and what the persistent kernel removes — a launch, grid drain and prologue
+// per GEMM, and the CTA-pair path's split-K reductions — is most of the time.
+// Larger problems keep one launch per GEMM on 256 x 256 CTA-pair tiles,
+// whose mainloop is the more efficient one.
+bool use_persistent(long long batch, long long m, const DeviceState& ds) {
+  const long long mt = (m + kBM - 1) / kBM;
+  return batch * (mt * (mt + 1) / 2) <= ds.sm_count;
 }
 
 // Full Newton-Schulz over a batch of same-shape matrices (batch = 1 for the
@@ -449,12 +572,21 @@ int ns_run(const void* G, int dtype, long long batch, long long rows, long long 
   if (workspace_bytes < w.bytes)
     return fail(FM_E_WORKSPACE, "workspace too small: need %zu bytes, got %llu", w.bytes,
                 (unsigned long long)workspace_bytes);
-  const NsPlan P = plan_ns(batch, m, n, g_gemm_path.load(std::memory_order_relaxed));
+  int path = g_gemm_path.load(std::memory_order_relaxed);
+  if (path == 0 && use_persistent(batch, m, *ds)) path = 4;
+  const bool persistent = path == 3 || path == 4;
+  const NsPlan P = plan_ns(batch, m, n, persistent ? 1 : path);
   auto* o = static_cast<__nv_bfloat16*>(out);
 
   const int pg = prep_grid(rows, cols, *ds);
   const long long tm = timer_begin(3, st);
-  if (P.split_slots > 0) FM_CUDA(cudaMemsetAsync(w.counters, 0, w.counter_bytes, st));
+  // Zero the counters a launch relies on before the normalisation kernels,
+  // so the kernels that follow them keep their programmatic overlap.
+  if (persistent && steps > 0) {
+    FM_CUDA(cudaMemsetAsync(w.phase, 0, kFusedSlots * sizeof(int), st));
+  } else if (P.split_slots > 0 && steps > 0) {
+    FM_CUDA(cudaMemsetAsync(w.counters, 0, w.counter_bytes, st));
+  }
   const long long bs_g_eff = batch > 1 ? bs_g : 0;
   FM_CUDA(launch_pdl(sumsq_kernel, dim3(pg, unsigned(batch)), dim3(kPrepThreads), 0, st, false,
                      G, dtype, rows, cols, ldg, bs_g_eff, w.partials));
@@ -479,6 +611,11 @@ int ns_run(const void* G, int dtype, long long batch, long long rows, long long 
   }
   FM_CUDA(cudaGetLastError());
   timer_end(tm, st);
+  if (persistent) {
+    const long long out_ld = tall ? m : n;
+    return path == 3 ? run_fused<256>(*ds, w, batch, m, n, steps, o, out_ld, bs_out, tall, st)
+                     : run_fused<128>(*ds, w, batch, m, n, steps, o, out_ld, bs_out, tall, st);
+  }
   for (int i = 0; i < steps; ++i) {
     const bool last = i == steps - 1;
     IterIO io;
@@ -668,7 +805,7 @@ int fm_muon_apply(void* param, int dtype, const void* update, int64_t n, float d
 }
 
 int fm_set_gemm_path(int path) {
-  if (path < 0 || path > 2) return fail(FM_E_INVALID, "gemm path must be 0, 1 or 2, got %d", path);
+  if (path < 0 || path > 4) return fail(FM_E_INVALID, "gemm path must be in [0, 4], got %d", path);
   g_gemm_path.store(path);
   return FM_OK;
 }
@@ -780,7 +917,7 @@ int fm_selftest_wait_timeout(void* stream) {
   g.out = operand[dev]; g.ld_out = 8;
   g.batch = 1; g.tiles = 1; g.split = 1; g.kb_per_split = 1;
   g.starve = 1;
-  return launch_gemm<kSyrk>(*ds, map, map, g, static_cast<cudaStream_t>(stream));
+  return launch_gemm<kSyrk>(*ds, map, map, map, g, static_cast<cudaStream_t>(stream));
 }
 
 int fm_device_error(uint32_t* code) {
@@ -803,6 +940,12 @@ int fm_device_error(uint32_t* code) {
 extern "C" int fm_trace_read(void* host) {
   FM_CUDA(cudaDeviceSynchronize());
   FM_CUDA(cudaMemcpyFromSymbol(host, fm::g_fm_trace, sizeof(fm::g_fm_trace)));
+  return FM_OK;
+}
+// Development only: the persistent kernel's timeline (160 x 64 x 4 u64).
+extern "C" int fm_fused_trace_read(void* host) {
+  FM_CUDA(cudaDeviceSynchronize());
+  FM_CUDA(cudaMemcpyFromSymbol(host, fm::g_fused_trace, sizeof(fm::g_fused_trace)));
   return FM_OK;
 }
 #endif

@@ -29,7 +29,7 @@ constexpr int kPairStages = 6;
 constexpr int kPairTileA = 128 * kBK * 2;  // 16 KB: this CTA's A rows
 constexpr int kPairTileB = 128 * kBK * 2;  // 16 KB: this CTA's half of B
 constexpr int kPairStageBytes = kPairTileA + kPairTileB;
-constexpr int kPairSmemBytes = kPairStages * kPairStageBytes + 1024 + 256 + kTBufBytes;
+constexpr int kPairSmemBytes = kPairStages * kPairStageBytes + 1024 + 256 + kEpiStageBytes;
 
 // Lower-triangle 256 x 256 tiles of an m x m matrix: T(T+1)/2, T = ceil(m/256).
 __host__ __device__ inline int syrk_pair_tile_count(int m) {
@@ -91,7 +91,8 @@ __device__ unsigned long long g_fm_trace[3][128][40];
 template <int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
     ns_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA,
-                        const __grid_constant__ CUtensorMap tmB, const GemmArgs g) {
+                        const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ CUtensorMap tmO, const GemmArgs g) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -102,8 +103,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* accf_bar = empty_bar + kPairStages;  // accumulator ready  [2]
   uint64_t* acce_bar = accf_bar + 2;             // accumulator drained [2] (leader's used)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce_bar + 2);
-  // per-warp transpose buffers of the epilogue, after the 256-byte barrier block
-  __nv_bfloat16* tbuf = reinterpret_cast<__nv_bfloat16*>(smem + kPairStages * kPairStageBytes + 256);
+  // per-warp epilogue staging buffers, after the 256-byte barrier block
+  __nv_bfloat16* sbuf = reinterpret_cast<__nv_bfloat16*>(smem + kPairStages * kPairStageBytes + 256);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -247,7 +248,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t acce_remote = mapa_shared(smem_u32(&acce_bar[acc]), 0);
       if (g.split == 1) {
         if (!epilogue_tile<MODE>(gb, tacc, q, row0w, col0, lane, out_vec, aux_vec, &accf_bar[acc],
-                                 acc_phase, abort_flag, tbuf + (warp - 2) * 32 * kTPitch))
+                                 acc_phase, abort_flag, sbuf + (warp - 2) * (kEpiWarpBytes / 2),
+                                 &tmO, w.b))
           break;
         if (lane == 0) mbar_arrive_remote(acce_remote);
         if (lane == 0 && q == 2 && rank == 0) FM_TRACE_MARK(3 + 3 * nunit);
@@ -282,7 +284,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (last) {
           __threadfence();
           epilogue_tile<MODE, true>(gb, 0, q, row0w, col0, lane, out_vec, aux_vec, nullptr, 0,
-                                    abort_flag, tbuf + (warp - 2) * 32 * kTPitch, parts, g.split);
+                                    abort_flag, sbuf + (warp - 2) * (kEpiWarpBytes / 2), &tmO,
+                                    w.b, parts, g.split);
         }
       }
       if (++acc == 2) {
@@ -290,6 +293,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         acc_phase ^= 1;
       }
     }
+    if (lane == 0) bulk_wait_all();  // TMA stores done before the CTA exits
+    __syncwarp();
   }
 
   tc_fence_before();

@@ -44,8 +44,13 @@ constexpr int kTileABytes = kBM * kBK * 2;  // 16 KB
 constexpr int kTileBBytes = kBN * kBK * 2;  // 32 KB
 constexpr int kStageBytes = kTileABytes + kTileBBytes;
 constexpr int kTmemCols = 2 * kBN;  // two fp32 accumulators
+// Epilogue staging in shared memory, per epilogue warp: two parities x
+// {row-major, transposed} 32 x 32 bf16 blocks that TMA stores write out.
+constexpr int kEpiBlock = 32 * 32;                  // elements of one block
+constexpr int kEpiWarpBytes = 4 * kEpiBlock * 2;    // 8 KB per warp
+constexpr int kEpiStageBytes = 4 * kEpiWarpBytes;   // 32 KB for the 4 epilogue warps
 constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align slack*/ + 256 /*barriers*/ +
-                           4 * 32 * 34 * 2 /*transpose buffers, kTBufBytes*/;
+                           kEpiStageBytes;
 
 // Newton-Schulz quintic coefficients (reference muon_fused/ns_step.py:39).
 constexpr float kNsA = 3.4445f;
@@ -77,6 +82,8 @@ struct GemmArgs {
   int* counters;      // split > 1: arrivals per (matrix, tile, CTA), zero between uses
   int starve;         // self-test only: the producer issues no loads, so the MMA
                       // warp's bounded wait must run out and report kErrWaitFull
+  int tma_out;        // 1: `out` is described by the kernel's store tensor map
+                      // (16-byte aligned rows); the epilogue writes through it
 };
 
 // A GemmArgs whose pointers address matrix b of the batch.
@@ -212,10 +219,10 @@ __device__ __forceinline__ void store_row32(__nv_bfloat16* rowp, int c0, int nco
   }
 }
 
-// Per-warp shared buffer for 32 x 32 transposed stores: rows of 34 bf16
-// (17 words, odd, so the row-wise 4-byte writes hit 32 distinct banks).
+// Per-warp shared buffer for 32 x 32 transposed stores of the direct-store
+// fallback: rows of 34 bf16 (17 words, odd, so the row-wise 4-byte writes hit
+// 32 distinct banks).  It lives in the warp's staging area.
 constexpr int kTPitch = 34;
-constexpr int kTBufBytes = 4 * 32 * kTPitch * 2;  // four epilogue warps
 
 // out[(c0 + l) * ld + row0w + j] = v_j[l] for the warp's 32 rows j and the
 // chunk's 32 columns l: the chunk goes through shared memory so that each lane
@@ -241,12 +248,35 @@ __device__ __forceinline__ void store_transposed32(__nv_bfloat16* out, long long
   for (int q = 0; q < 4; ++q) dst[q] = reinterpret_cast<const uint4*>(o)[q];
 }
 
+// Staging of one 32 x 32 chunk for a TMA store.  Lane r holds row r of the
+// chunk in v.  Row-major: row r is 64 contiguous bytes.  Transposed: element
+// (r, k) goes to (k, r), so each store instruction of the warp writes 64
+// contiguous bytes.  Symmetric: the block on the diagonal of a SYRK output,
+// built from its lower triangle only (what the direct-store path writes).
+__device__ __forceinline__ void stage_rows32(__nv_bfloat16* blk, int lane, const float (&v)[32]) {
+  uint4* d = reinterpret_cast<uint4*>(blk + lane * 32);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) d[q] = pack8_bf16(v + 8 * q);
+}
+__device__ __forceinline__ void stage_cols32(__nv_bfloat16* blk, int lane, const float (&v)[32]) {
+#pragma unroll
+  for (int k = 0; k < 32; ++k) blk[k * 32 + lane] = __float2bfloat16_rn(v[k]);
+}
+__device__ __forceinline__ void stage_sym32(__nv_bfloat16* blk, int lane, const float (&v)[32]) {
+#pragma unroll
+  for (int k = 0; k < 32; ++k) {
+    const __nv_bfloat16 h = __float2bfloat16_rn(v[k]);
+    if (k <= lane) blk[lane * 32 + k] = h;
+    if (k < lane) blk[k * 32 + lane] = h;
+  }
+}
+
 // Number of 32-column chunks of a tile row block that warp rows row0w.. store:
 // a prefix (columns below N; for the SYRK modes also at or left of the warp's
 // last row).
-template <int MODE>
+template <int MODE, int TBN = kBN>
 __device__ __forceinline__ int epilogue_chunks(const GemmArgs& g, int row0w, int col0) {
-  int col_end = min(g.N, col0 + kBN);
+  int col_end = min(g.N, col0 + TBN);
   if constexpr (MODE != kBX) col_end = min(col_end, row0w + 32);
   return row0w < g.M ? max(0, (col_end - col0 + 31) / 32) : 0;
 }
@@ -285,21 +315,30 @@ __device__ __forceinline__ bool stash_partial(const GemmArgs& g, uint32_t tmem_a
 // row0w .. row0w+31; the tile's columns start at col0.
 //   FROM_PARTIALS = false: values come from the TMEM accumulator at tmem_acc,
 //     after waiting on accf_bar (parity acc_phase); returns false if that
-//     wait gave up.  Shared by the 1-CTA and the 2-CTA kernels.
+//     wait gave up.  Shared by the 1-CTA, 2-CTA and persistent kernels.
 //   FROM_PARTIALS = true: values are the sum, in split order, of `split`
 //     fp32 partials starting at `parts` (stride kPartialFloats) — the
 //     last-arriving split of a split-K tile runs this.
-template <int MODE, bool FROM_PARTIALS = false>
+// Stores: with g.tma_out, each 32 x 32 chunk is staged in the warp's shared
+// buffers `sbuf` (8 KB: two parities x {row-major, transposed}) and written
+// by TMA tile stores through `tm_out` at matrix index `bz`; lane 0 issues
+// them and keeps at most one older chunk's stores in flight, so the warp
+// moves on while the copies drain.  Otherwise every lane stores its own row
+// (unaligned outputs).  The caller waits for outstanding stores
+// (bulk_wait_all) before the results are consumed or the CTA exits.
+template <int MODE, bool FROM_PARTIALS = false, int TBN = kBN>
 __device__ __forceinline__ bool epilogue_tile(const GemmArgs& g, uint32_t tmem_acc, int q,
                                               int row0w, int col0, int lane, bool out_vec,
                                               bool aux_vec, uint64_t* accf_bar, uint32_t acc_phase,
                                               volatile int* abort_flag,
-                                              __nv_bfloat16* tbuf,
-                                              const float* parts = nullptr, int split = 1) {
+                                              __nv_bfloat16* sbuf, const CUtensorMap* tm_out,
+                                              int bz, const float* parts = nullptr,
+                                              int split = 1) {
   const int row = row0w + lane;
   const bool row_ok = row < g.M;
   const __nv_bfloat16* aux_row = g.aux + static_cast<long long>(row) * g.ld_aux;
-  const int nc = epilogue_chunks<MODE>(g, row0w, col0);
+  const int nc = epilogue_chunks<MODE, TBN>(g, row0w, col0);
+  const bool use_tma = g.tma_out != 0;
   // The epilogue operand (A for kPoly, X for kBX) does not depend on the
   // accumulator: fetch the first chunk before waiting for the MMAs and each
   // next chunk while the current one is processed.
@@ -331,9 +370,6 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& g, uint32_t tmem_a
     } else {
       tmem_ld_32x32b_x32(tmem_acc + c * 32 + (static_cast<uint32_t>(q * 32) << 16), v);
     }
-    // All 32 rows and columns of this chunk in bounds (warp-uniform): the
-    // column-wise stores (mirror, transposed output) can go through smem.
-    const bool whole = row0w + 31 < g.M && c0 + 31 < g.N && out_vec;
     if constexpr (MODE == kPoly) {
       if (row_ok) {
         float av[32];
@@ -350,32 +386,67 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& g, uint32_t tmem_a
         }
       }
     }
-    if constexpr (MODE != kBX) {
-      if (row_ok) store_row32(g.out + row * g.ld_out, c0, g.N, row, true, out_vec, v);
-      if (whole && c0 + 31 < row0w) {  // chunk strictly below the diagonal
-        store_transposed32(g.out, g.ld_out, row0w, c0, lane, tbuf, v);
-      } else if (row_ok) {
-        store_mirror32(g.out, g.ld_out, c0, g.N, row, v);
-      }
-    } else {
+    if constexpr (MODE == kBX) {
       float xv[32];
 #pragma unroll
       for (int k = 0; k < 4; ++k) unpack8_bf16(araw[k], xv + 8 * k);
 #pragma unroll
       for (int k = 0; k < 32; ++k) v[k] = fmaf(dval, xv[k], v[k]);
-      if (g.transpose_out) {
-        if (whole) {
-          store_transposed32(g.out, g.ld_out, row0w, c0, lane, tbuf, v);
-        } else if (row_ok) {
-#pragma unroll
-          for (int k = 0; k < 32; ++k) {
-            const int col = c0 + k;
-            if (col < g.N)
-              g.out[static_cast<long long>(col) * g.ld_out + row] = __float2bfloat16_rn(v[k]);
-          }
+    }
+    if (use_tma) {
+      __nv_bfloat16* bd = sbuf + (c & 1) * 2 * kEpiBlock;
+      __nv_bfloat16* bt = bd + kEpiBlock;
+      if (lane == 0) bulk_wait_read<1>();  // chunk c-2's stores have read this parity
+      __syncwarp();
+      bool st_rows = true, st_cols = false;
+      if constexpr (MODE != kBX) {
+        if (c0 == row0w) {
+          stage_sym32(bd, lane, v);  // diagonal block, symmetric
+        } else {
+          stage_rows32(bd, lane, v);  // strictly below the diagonal: direct + mirror
+          stage_cols32(bt, lane, v);
+          st_cols = true;
         }
-      } else if (row_ok) {
-        store_row32(g.out + row * g.ld_out, c0, g.N, row, false, out_vec, v);
+      } else if (g.transpose_out) {
+        stage_cols32(bt, lane, v);
+        st_rows = false;
+        st_cols = true;
+      } else {
+        stage_rows32(bd, lane, v);
+      }
+      fence_proxy_async_shared();
+      __syncwarp();
+      if (lane == 0) {
+        if (st_rows) tma_store_3d(tm_out, bd, c0, row0w, bz);
+        if (st_cols) tma_store_3d(tm_out, bt, row0w, c0, bz);
+        bulk_commit();
+      }
+    } else {
+      // All 32 rows and columns of this chunk in bounds (warp-uniform): the
+      // column-wise stores (mirror, transposed output) can go through smem.
+      const bool whole = row0w + 31 < g.M && c0 + 31 < g.N && out_vec;
+      if constexpr (MODE != kBX) {
+        if (row_ok) store_row32(g.out + row * g.ld_out, c0, g.N, row, true, out_vec, v);
+        if (whole && c0 + 31 < row0w) {  // chunk strictly below the diagonal
+          store_transposed32(g.out, g.ld_out, row0w, c0, lane, sbuf, v);
+        } else if (row_ok) {
+          store_mirror32(g.out, g.ld_out, c0, g.N, row, v);
+        }
+      } else {
+        if (g.transpose_out) {
+          if (whole) {
+            store_transposed32(g.out, g.ld_out, row0w, c0, lane, sbuf, v);
+          } else if (row_ok) {
+#pragma unroll
+            for (int k = 0; k < 32; ++k) {
+              const int col = c0 + k;
+              if (col < g.N)
+                g.out[static_cast<long long>(col) * g.ld_out + row] = __float2bfloat16_rn(v[k]);
+            }
+          }
+        } else if (row_ok) {
+          store_row32(g.out + row * g.ld_out, c0, g.N, row, false, out_vec, v);
+        }
       }
     }
     if constexpr (MODE != kSyrk) {
@@ -391,7 +462,7 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs& g, uint32_t tmem_a
 template <int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
     ns_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const GemmArgs g) {
+                   const __grid_constant__ CUtensorMap tmO, const GemmArgs g) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 128B-swizzled TMA destinations need 1024-byte alignment.
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -403,8 +474,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* accf_bar = empty_bar + kStages;  // accumulator ready  [2]
   uint64_t* acce_bar = accf_bar + 2;         // accumulator drained [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce_bar + 2);
-  // per-warp transpose buffers of the epilogue, after the 256-byte barrier block
-  __nv_bfloat16* tbuf = reinterpret_cast<__nv_bfloat16*>(smem + kStages * kStageBytes + 256);
+  // per-warp epilogue staging buffers, after the 256-byte barrier block
+  __nv_bfloat16* sbuf = reinterpret_cast<__nv_bfloat16*>(smem + kStages * kStageBytes + 256);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -537,7 +608,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tile_coords<MODE>(g, t, ti, tj);
       if (!epilogue_tile<MODE>(g, tmem_base + acc * kBN, q, ti * kBM + q * 32, tj * kBN, lane,
                                out_vec, aux_vec, &accf_bar[acc], acc_phase, abort_flag,
-                               tbuf + (warp - 2) * 32 * kTPitch))
+                               sbuf + (warp - 2) * (kEpiWarpBytes / 2), &tmO, 0))
         break;
       if (lane == 0) mbar_arrive(&acce_bar[acc]);
       if (++acc == 2) {
@@ -545,6 +616,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         acc_phase ^= 1;
       }
     }
+    if (lane == 0) bulk_wait_all();  // TMA stores done before the CTA exits
+    __syncwarp();
   }
 
   __syncthreads();
