@@ -266,8 +266,11 @@ class FusedMuon(Optimizer):
             self._apply_update(params[i], u, group["lr"], group["wd"])
 
         dev = params[0].device
-        if self._collective == "param_gather" and sharding.ParamStore.supports(params):
-            store = self._stores.get(key)
+        store = self._stores.get(key)
+        if self._collective == "param_gather" and (store is not None
+                                                   or sharding.ParamStore.supports(params)):
+            # supports() is checked before the store exists: afterwards the
+            # parameters deliberately share the store's flat buffers
             if store is None:
                 store = sharding.ParamStore(plan, params, dev)
                 self._stores[key] = store

@@ -82,8 +82,19 @@ def _worker(rank, world, port, outdir, bucket_bytes, leave_rank, collective="ncc
             dist.destroy_process_group()
             return
         ids = [id(p) for p in params]
+        if collective == "param_gather":
+            from muon_fused import sharding
+
+            def _no_fallback(*a, **k):
+                raise AssertionError("param_gather step fell back to the update all-gather")
+
+            sharding.run_sharded = _no_fallback  # every step must take the in-place exchange
         opt = _run_steps(params, 2, bucket_bytes, collective)
         assert [id(p) for p in opt.param_groups[0]["params"]] == ids  # same Parameter objects
+        if collective == "param_gather":
+            # the parameters still live in the store's flat buffers
+            store = next(iter(opt._stores.values()))
+            assert all(p.data_ptr() == s.data_ptr() for p, s in zip(params, store.slots))
         owned = sorted(i for i, p in enumerate(params) if "momentum_buffer" in opt.state[p])
         torch.save({"params": [p.detach().clone() for p in params], "owned": owned},
                    os.path.join(outdir, f"rank{rank}.pt"))
