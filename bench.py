@@ -20,6 +20,10 @@ Workloads:
           (benchmarks/bench_ns_step.py:41-81: 200 warm-ups, 50 timed calls,
           median), beside the reference's PyTorch NS on the same GPU, eager
           and under torch.compile.  One JSON line per shape.
+  prep    the normalisation / transpose kernels alone, HBM GB/s per shape.
+  gemm_compare  each NS GEMM alone against cuBLAS (torch.mm) doing the same
+          product, per shape (default (4096,4096), (4096,14336), (2048,8192));
+          --sweep-shapes picks others.  One JSON line per shape.
 
 The metric is dense-equivalent Newton-Schulz TFLOP/s (the reference's count,
 5·(4m²n + 2m³) per matrix; docs/optimization_report.md:24-29), whole job, max
@@ -358,13 +362,19 @@ def bench_ns(args, peaks, peak_src):
             if k in stage_flops:
                 d["dense_eq_tflops"] = round(stage_flops[k] / (avg * 1e-3) / 1e12, 1)
             stages[k] = d
-    dom = "gemm3_bx"
+    if st["gemm3_bx"][1]:
+        dom = "gemm3_bx"
+        kname = "ns_gemm_pair_kernel<kBX> (X' = d*X + Boff*X)"
+    else:
+        # small problems run all iterations in the persistent kernel: it is
+        # the dominant (only) tensor kernel, credited with the whole NS
+        dom = "fused_ns"
+        stage_flops[dom] = ns_flops(m, n)
+        kname = "ns_fused_kernel<128> (all 5 iterations, 128x128 tiles)"
     avg_dom = st[dom][0] / st[dom][1]
     achieved = stage_flops[dom] / (avg_dom * 1e-3) / 1e12
     peak = float(peaks["bf16_tflops"])
-    roofline = {"bound": "tensor",
-                "kernel": ("ns_gemm_pair_kernel<kBX>" if mo > 256 else "ns_gemm_kernel<kBX>")
-                + " (X' = d*X + Boff*X)",
+    roofline = {"bound": "tensor", "kernel": kname,
                 "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
                 "frac": round(achieved / peak, 4), "peak_source": f"{peak_src} bf16_tflops (burst)",
                 "traffic": None, "stages": stages}
@@ -681,6 +691,115 @@ def bench_sweep(args, peaks, peak_src):
     return lines
 
 
+GEMM_COMPARE_SHAPES = [(4096, 4096), (4096, 14336), (2048, 8192)]
+
+
+def bench_gemm_compare(args, peaks, peak_src):
+    """Each Newton-Schulz GEMM alone against cuBLAS (torch.mm, bf16) doing the
+    same product on the same B200, per (m, n): GEMM1 A = X·Xᵀ (m x m, K = n),
+    GEMM2 A·A (m x m, K = m), GEMM3 B·X (m x n, K = m).  Ours: one
+    newton_schulz_step per call with per-launch CUDA events around each GEMM
+    (fm_stage_timing); cuBLAS: CUDA events around torch.mm.  Ours computes only
+    the lower triangle of the two SYRKs and fuses its epilogues; the TFLOP/s
+    columns use the dense product's 2·M·N·K for both, so they compare times at
+    equal work.  Medians over 30 calls after 20 warm-ups, clocks sampled."""
+    from muon_fused import _fused_muon_C as _C
+    from muon_fused import _lib
+
+    dev = torch.device("cuda")
+    peak = float(peaks["bf16_tflops"])
+    for m, n in (args.sweep_shapes or GEMM_COMPARE_SHAPES):
+        gen = torch.Generator(device=dev).manual_seed(0)
+        X = torch.randn(m, n, generator=gen, device=dev, dtype=torch.bfloat16)
+        X = (X.float() / X.float().norm()).bfloat16()
+        ws = torch.empty(_C.workspace_size(m, max(m, n)), dtype=torch.uint8, device=dev)
+        A = X @ X.T
+        B = torch.randn(m, m, generator=gen, device=dev, dtype=torch.bfloat16)
+        with ClockSampler(torch.cuda.current_device()) as clk:
+            for _ in range(20):
+                _C.newton_schulz_step(X, ws)
+            torch.cuda.synchronize()
+            per = {k: [] for k in ("gemm1_syrk", "gemm2_poly", "gemm3_bx")}
+            for _ in range(30):
+                _lib.stage_timing(True)
+                _C.newton_schulz_step(X, ws)
+                st = _lib.stage_times()
+                for k in per:
+                    per[k].append(st[k][0] / max(st[k][1], 1))
+            _lib.stage_timing(False)
+            ours = {k: statistics.median(v) for k, v in per.items()}
+
+            def mm_ms(a, b):
+                for _ in range(20):
+                    torch.mm(a, b)
+                torch.cuda.synchronize()
+                evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                       for _ in range(30)]
+                for s_, e_ in evs:
+                    s_.record()
+                    torch.mm(a, b)
+                    e_.record()
+                torch.cuda.synchronize()
+                return statistics.median(s_.elapsed_time(e_) for s_, e_ in evs)
+
+            cub = {"gemm1_syrk": mm_ms(X, X.T), "gemm2_poly": mm_ms(A, A),
+                   "gemm3_bx": mm_ms(B, X)}
+        flops = {"gemm1_syrk": 2.0 * m * m * n, "gemm2_poly": 2.0 * m ** 3,
+                 "gemm3_bx": 2.0 * m * m * n}
+        line = {"workload": "gemm_compare", "shape": [m, n], "clocks": clk.summary(),
+                "peak": f"{peak} TFLOP/s ({peak_src} bf16_tflops, burst)"}
+        for k in flops:
+            line[k] = {"ours_us": round(ours[k] * 1e3, 2), "cublas_us": round(cub[k] * 1e3, 2),
+                       "ours_dense_eq_tflops": round(flops[k] / (ours[k] * 1e-3) / 1e12, 1),
+                       "cublas_tflops": round(flops[k] / (cub[k] * 1e-3) / 1e12, 1),
+                       "ratio_cublas_over_ours": round(cub[k] / ours[k], 3)}
+        print(json.dumps(line), flush=True)
+
+
+PREP_SHAPES = [(1, 4096, 4096), (1, 4096, 14336), (1, 14336, 4096), (8, 14336, 4096),
+               (64, 1024, 4096), (1, 896, 1152)]
+
+
+def bench_prep(args, peaks, peak_src):
+    """The normalisation kernels alone (HBM-bound): sum of squares of bf16(G)
+    and the scaled copy X0 = bf16(bf16(G) / (||G||_F + 1e-7)), transposed for
+    tall inputs.  Algorithmic bytes per matrix: 2mn read for the norm, 2mn
+    read + 2mn write for the copy (bf16 input).  Per shape (batch, rows,
+    cols): the prep kernels' summed CUDA-event time per call (fm_stage_timing
+    stage "prep"), averaged over 20 calls of a 1-step Newton-Schulz after 5
+    warm-ups, L2 flushed (256 MB write) before each call."""
+    from muon_fused import _fused_muon_C as _C
+    from muon_fused import _lib
+
+    dev = torch.device("cuda")
+    peak = float(peaks["hbm_gbs"])
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    for b, r, c in PREP_SHAPES:
+        G = torch.randn(b, r, c, generator=torch.Generator(device=dev).manual_seed(0),
+                        device=dev, dtype=torch.bfloat16)
+        ws = torch.empty(_C.workspace_size_batched(b, r, c), dtype=torch.uint8, device=dev)
+        out = torch.empty_like(G)
+        for _ in range(5):
+            _C.fused_newton_schulz_batched(G, 1, ws, out=out)
+        torch.cuda.synchronize()
+        tot = 0.0
+        for _ in range(20):
+            flush_l2(flush)
+            _lib.stage_timing(True)
+            _C.fused_newton_schulz_batched(G, 1, ws, out=out)
+            tot += _lib.stage_times()["prep"][0]
+        _lib.stage_timing(False)
+        ms = tot / 20
+        nbytes = 6.0 * b * r * c
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        print(json.dumps({"workload": "prep", "batch": b, "shape": [r, c],
+                          "kernels": "sumsq + " + ("scale_transpose" if r > c else "scale"),
+                          "us": round(ms * 1e3, 2), "algorithmic_bytes": int(nbytes),
+                          "gbs": round(gbs, 1), "frac_of_hbm": round(gbs / peak, 4),
+                          "peak": f"{peak} GB/s ({peak_src} hbm_gbs)"}), flush=True)
+        del G, ws, out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -688,7 +807,9 @@ def main():
                     help="timed steps (default: 400 for ns, 40 for the optimizer-step workloads, "
                          "so the timed work stays within about a minute)")
     ap.add_argument("--warmup", type=int, default=20)
-    ap.add_argument("--workload", choices=["ns", "muon1b", "muon8b", "sweep"], default="muon8b")
+    ap.add_argument("--workload",
+                    choices=["ns", "muon1b", "muon8b", "sweep", "gemm_compare", "prep"],
+                    default="muon8b")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--collective", choices=["nccl", "param_gather"], default="param_gather",
                     help="sharded-step exchange: all-gather of the updates + apply on every "
@@ -725,9 +846,10 @@ def main():
 
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
     peaks, peak_src = load_peaks()
-    if args.workload == "sweep":
+    if args.workload in ("sweep", "gemm_compare", "prep"):
         if rank == 0:
-            bench_sweep(args, peaks, peak_src)
+            {"sweep": bench_sweep, "gemm_compare": bench_gemm_compare,
+             "prep": bench_prep}[args.workload](args, peaks, peak_src)
         if world > 1:
             import torch.distributed as dist
 
@@ -740,11 +862,13 @@ def main():
         r["ms"] = barrier_max(r["ms"], world)
         value = world * r["flops"] / (r["ms"] * 1e-3) / 1e12
     else:
+        # the (4096, 4096) sub-measurement first, on a fresh process state
+        # (its pipelined end-to-end copies are sensitive to what ran before)
+        if world == 1 and not args.no_ns_headline:
+            ns_sub = ns_headline(args, peaks, peak_src)
+            torch.cuda.empty_cache()
         r = bench_muon(args, world, rank, peaks, peak_src)
         value = r["flops"] / (r["ms"] * 1e-3) / 1e12
-        if world == 1 and not args.no_ns_headline:
-            torch.cuda.empty_cache()
-            ns_sub = ns_headline(args, peaks, peak_src)
 
     if rank == 0:
         line = {

@@ -170,7 +170,12 @@ int fm_muon_apply(void* param, int dtype, const void* update, int64_t n, float d
 
 /*
  * GEMM kernel selection for all later calls in the process:
- * 0 = automatic, 1 = one launch per GEMM with single-CTA 128x256 tiles,
+ * 0 = automatic: a single-matrix call (fm_fused_newton_schulz, the
+ *     allocation-free form) whose lower-triangle 128x128 tiles fit on the SMs
+ *     runs the persistent kernel (path 4, one cooperative launch for all
+ *     iterations); everything else, and every batched call, runs one launch
+ *     per GEMM on CTA-pair tiles (single-CTA tiles for unbatched m <= 256),
+ * 1 = one launch per GEMM with single-CTA 128x256 tiles,
  * 2 = one launch per GEMM with CTA-pair 256x256 tiles, 3 = one persistent
  * launch for all iterations with 128x256 tiles, 4 = the same with 128x128
  * tiles.  All produce the same arithmetic (up to fp32 summation order where a

@@ -551,9 +551,14 @@ bool use_persistent(long long batch, long long m, const DeviceState& ds) {
 
 // Full Newton-Schulz over a batch of same-shape matrices (batch = 1 for the
 // single-matrix entry points).
+// auto_persistent: whether the automatic path may pick the persistent kernel.
+// Only the single-matrix entry points allow it.  The persistent kernel is a
+// cooperative launch (all CTAs resident at once), so while other kernels hold
+// SMs — e.g. NCCL collectives on another stream beside a sharded optimizer
+// step, which uses the batched entry — it would wait for them to finish.
 int ns_run(const void* G, int dtype, long long batch, long long rows, long long cols, long long ldg,
            long long bs_g, void* out, long long bs_out, int steps, void* workspace,
-           uint64_t workspace_bytes, cudaStream_t st) {
+           uint64_t workspace_bytes, cudaStream_t st, bool auto_persistent) {
   if (!G || !out || !workspace) return fail(FM_E_INVALID, "null pointer argument");
   if (dtype < FM_DT_BF16 || dtype > FM_DT_F64) return fail(FM_E_INVALID, "unknown dtype %d", dtype);
   if (steps < 0) return fail(FM_E_INVALID, "steps must be >= 0, got %d", steps);
@@ -573,7 +578,7 @@ int ns_run(const void* G, int dtype, long long batch, long long rows, long long 
     return fail(FM_E_WORKSPACE, "workspace too small: need %zu bytes, got %llu", w.bytes,
                 (unsigned long long)workspace_bytes);
   int path = g_gemm_path.load(std::memory_order_relaxed);
-  if (path == 0 && use_persistent(batch, m, *ds)) path = 4;
+  if (path == 0 && auto_persistent && use_persistent(batch, m, *ds)) path = 4;
   const bool persistent = path == 3 || path == 4;
   const NsPlan P = plan_ns(batch, m, n, persistent ? 1 : path);
   auto* o = static_cast<__nv_bfloat16*>(out);
@@ -661,7 +666,7 @@ int fm_fused_newton_schulz(const void* G, int dtype, int64_t rows, int64_t cols,
                            void* out, int steps, void* workspace, uint64_t workspace_bytes,
                            void* stream) {
   return ns_run(G, dtype, 1, rows, cols, ldg, 0, out, rows * cols, steps, workspace,
-                workspace_bytes, static_cast<cudaStream_t>(stream));
+                workspace_bytes, static_cast<cudaStream_t>(stream), true);
 }
 
 int fm_fused_newton_schulz_batched(const void* G, int dtype, int64_t batch, int64_t rows,
@@ -669,7 +674,7 @@ int fm_fused_newton_schulz_batched(const void* G, int dtype, int64_t batch, int6
                                    int64_t batch_stride_out, int steps, void* workspace,
                                    uint64_t workspace_bytes, void* stream) {
   return ns_run(G, dtype, batch, rows, cols, ldg, batch_stride_g, out, batch_stride_out, steps,
-                workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+                workspace, workspace_bytes, static_cast<cudaStream_t>(stream), false);
 }
 
 static int step_common(const void* X, int64_t m, int64_t n, int64_t ldx, void* X_new,
