@@ -605,7 +605,7 @@ int ns_run(const void* G, int dtype, long long batch, long long rows, long long 
     return FM_OK;
   }
   if (tall) {
-    dim3 grid(unsigned((cols + kTT - 1) / kTT), unsigned((rows + kTT - 1) / kTT), unsigned(batch));
+    dim3 grid(unsigned((cols + kTC - 1) / kTC), unsigned((rows + kTR - 1) / kTR), unsigned(batch));
     FM_CUDA(launch_pdl(scale_transpose_kernel, grid, dim3(kPrepThreads), 0, st, false, G, dtype,
                        rows, cols, ldg, bs_g_eff, (const float*)w.partials, pg, w.X[0], w.ldx,
                        w.xs));

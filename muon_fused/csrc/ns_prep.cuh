@@ -124,10 +124,28 @@ struct ChunkWalk {
 // of 0x8000, where the exact division decides (Ziv's strategy: a cheap
 // approximation, a rounding test, an exact fallback for the rare hard case).
 // Also exact for zeros, infinities, NaNs and subnormal quotients.
-__device__ __forceinline__ float div_for_bf16(float x, float den, float rcp) {
-  const float q = x * rcp;
-  const int low = static_cast<int>(__float_as_uint(q) & 0xFFFFu);
-  return abs(low - 0x8000) <= 16 ? x / den : q;
+__device__ __forceinline__ bool near_bf16_midpoint(float q) {
+  return (((__float_as_uint(q) & 0xFFFFu) - 0x7FF0u) & 0xFFFFu) <= 32u;
+}
+
+// The rule above over an 8-element chunk.  The exact division runs in a
+// warp-uniform branch taken only when some lane of the warp has a hard case
+// (a ternary select let the compiler compute the division for every element).
+__device__ __forceinline__ void div8_for_bf16(float (&x)[8], float den, float rcp) {
+  float q[8];
+  bool hard = false;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    q[k] = x[k] * rcp;
+    hard |= near_bf16_midpoint(q[k]);
+  }
+  if (__any_sync(__activemask(), hard)) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      if (near_bf16_midpoint(q[k])) q[k] = __fdiv_rn(x[k], den);
+  }
+#pragma unroll
+  for (int k = 0; k < 8; ++k) x[k] = q[k];
 }
 
 // Load chunk (r, c) as bf16-rounded floats (zero beyond cols).
@@ -290,7 +308,7 @@ __global__ void __launch_bounds__(kPrepThreads, 4) scale_kernel(const void* __re
         float x[8];
         unpack8(raw[u], x);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) x[k] = div_for_bf16(x[k], den, rcp);
+        div8_for_bf16(x, den, rcp);
         dst[l] = pack8(x);
       }
     }
@@ -312,7 +330,7 @@ __global__ void __launch_bounds__(kPrepThreads, 4) scale_kernel(const void* __re
       if (w.r[u] >= r1) continue;
       const long long r = w.r[u], c = w.c[u];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) x[u][k] = div_for_bf16(x[u][k], den, rcp);
+      div8_for_bf16(x[u], den, rcp);
       __nv_bfloat16* dst = X + r * ldx + c * 8;
       if (vout && c * 8 + 8 <= cols) {
         *reinterpret_cast<uint4*>(dst) = pack8(x[u]);
@@ -327,13 +345,15 @@ __global__ void __launch_bounds__(kPrepThreads, 4) scale_kernel(const void* __re
 }
 
 // Transposing variant for tall G (rows > cols): X[c][r] = bf16(bf16(G[r][c]) / den).
-// 64x64 tiles through shared memory so both the read and the write coalesce.
-// Each thread issues both of its row-chunk loads before using either.  The
-// tile's row pitch of 66 elements (33 words) keeps the column-wise gathers of
-// the store phase to at most two-way bank conflicts (a pitch of 72 made them
-// eight-way) and the row-wise writes of the load phase conflict-free.
-constexpr int kTT = 64;
-constexpr int kTPitchT = kTT + 2;
+// Tiles of kTR rows x kTC columns of G go through shared memory so both the
+// read (rows of G) and the write (rows of X = columns of G) coalesce; each
+// thread has kPer 16-byte chunks in flight.  The tile's row pitch of kTC + 2
+// elements keeps the column-wise gathers of the store phase to at most
+// two-way bank conflicts and the row-wise writes of the load phase
+// conflict-free.
+constexpr int kTR = 64;    // rows of G per tile (= columns of the X tile)
+constexpr int kTC = 128;   // columns of G per tile (= rows of the X tile)
+constexpr int kTPitchT = kTC + 2;
 __global__ void __launch_bounds__(kPrepThreads) scale_transpose_kernel(
     const void* __restrict__ G0, int dtype, long long rows, long long cols, long long ldg,
     long long bs_g, const float* partials, int nparts, __nv_bfloat16* X, long long ldx,
@@ -343,43 +363,43 @@ __global__ void __launch_bounds__(kPrepThreads) scale_transpose_kernel(
   partials += static_cast<long long>(blockIdx.z) * kMaxPartials;
   X += static_cast<long long>(blockIdx.z) * xs;
   __shared__ float s_den;
-  __shared__ __nv_bfloat16 tile[kTT][kTPitchT];
-  const float den = nparts > 0 ? norm_denominator(partials, nparts, &s_den) : 1.f;
-  const float rcp = 1.f / den;
+  __shared__ __nv_bfloat16 tile[kTR][kTPitchT];
   const ChunkGrid g{rows, cols, ldg, (cols + 7) / 8};
   const bool vin = bf16_vec_ok(G, dtype, ldg);
   const bool vout = ((reinterpret_cast<uintptr_t>(X) | static_cast<uintptr_t>(ldx * 2)) & 15) == 0;
-  const long long r0 = static_cast<long long>(blockIdx.y) * kTT;
-  const long long c0 = static_cast<long long>(blockIdx.x) * kTT;
-  constexpr int kPer = kTT * (kTT / 8) / kPrepThreads;  // row chunks per thread (2)
-  // load: 64 rows x 8 chunks
+  const long long r0 = static_cast<long long>(blockIdx.y) * kTR;
+  const long long c0 = static_cast<long long>(blockIdx.x) * kTC;
+  constexpr int kPer = kTR * (kTC / 8) / kPrepThreads;  // chunks per thread (4)
+  // load: kTR rows x kTC/8 chunks, issued before the norm is reduced
   float x[kPer][8];
 #pragma unroll
   for (int j = 0; j < kPer; ++j) {
     const int i = threadIdx.x + j * kPrepThreads;
-    const long long r = r0 + i / (kTT / 8), cc = c0 / 8 + i % (kTT / 8);
-    if (r < rows) {
+    const long long r = r0 + i / (kTC / 8), cc = c0 / 8 + i % (kTC / 8);
+    if (r < rows && cc * 8 < cols) {
       load_chunk(G, dtype, g, vin, r, cc, x[j]);
     } else {
 #pragma unroll
       for (int k = 0; k < 8; ++k) x[j][k] = 0.f;
     }
   }
+  const float den = nparts > 0 ? norm_denominator(partials, nparts, &s_den) : 1.f;
+  const float rcp = 1.f / den;
 #pragma unroll
   for (int j = 0; j < kPer; ++j) {
     const int i = threadIdx.x + j * kPrepThreads;
-    const int tr = i / (kTT / 8), tc = i % (kTT / 8);
+    const int tr = i / (kTC / 8), tc = i % (kTC / 8);
+    div8_for_bf16(x[j], den, rcp);
 #pragma unroll
-    for (int k = 0; k < 8; ++k)
-      tile[tr][tc * 8 + k] = __float2bfloat16_rn(div_for_bf16(x[j][k], den, rcp));
+    for (int k = 0; k < 8; ++k) tile[tr][tc * 8 + k] = __float2bfloat16_rn(x[j][k]);
   }
   __syncthreads();
-  // store: output rows c0.. (64 of them) x 8 chunks along r
+  // store: output rows c0 .. c0+kTC-1, each kTR/8 chunks along r
 #pragma unroll
   for (int j = 0; j < kPer; ++j) {
     const int i = threadIdx.x + j * kPrepThreads;
-    const int orow = i / (kTT / 8), oc = i % (kTT / 8);
-    const long long c = c0 + orow;  // output row
+    const int orow = i / (kTR / 8), oc = i % (kTR / 8);
+    const long long c = c0 + orow;    // output row
     const long long r = r0 + oc * 8;  // first output column
     if (c >= cols) continue;
     __nv_bfloat16* dst = X + c * ldx + r;
