@@ -307,7 +307,6 @@ __global__ void __launch_bounds__(kPrepThreads, 4) scale_kernel(const void* __re
         if (l >= hi) continue;
         float x[8];
         unpack8(raw[u], x);
-#pragma unroll
         div8_for_bf16(x, den, rcp);
         dst[l] = pack8(x);
       }
@@ -329,7 +328,6 @@ __global__ void __launch_bounds__(kPrepThreads, 4) scale_kernel(const void* __re
     for (int u = 0; u < kUnroll; ++u) {
       if (w.r[u] >= r1) continue;
       const long long r = w.r[u], c = w.c[u];
-#pragma unroll
       div8_for_bf16(x[u], den, rcp);
       __nv_bfloat16* dst = X + r * ldx + c * 8;
       if (vout && c * 8 + 8 <= cols) {
