@@ -20,9 +20,12 @@ def _randn(shape, seed, scale=1.0):
     return (torch.randn(shape, generator=torch.Generator().manual_seed(seed)) * scale)
 
 
-@pytest.mark.parametrize("shape", [(1024, 2048), (1536, 768), (512, 2048), (300, 700)])
+@pytest.mark.parametrize("shape", [(1024, 2048), (1536, 768), (512, 2048), (300, 700),
+                                   (2560, 3072)])
 def test_ns_graph_replay_matches_eager(cuda_lib, shape):
-    """Wide, tall (transposing path), split-K and ragged shapes."""
+    """Wide, tall (transposing path) and ragged shapes on the persistent kernel
+    (a cooperative launch, captured like any other), and (2560, 3072) on the
+    per-GEMM CTA-pair kernels."""
     from muon_fused import fused_newton_schulz, workspace_size
 
     G = _randn(shape, 0).bfloat16().to(DEV)
