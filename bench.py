@@ -366,11 +366,14 @@ def bench_ns(args, peaks, peak_src):
         dom = "gemm3_bx"
         kname = "ns_gemm_pair_kernel<kBX> (X' = d*X + Boff*X)"
     else:
-        # small problems run all iterations in the persistent kernel: it is
-        # the dominant (only) tensor kernel, credited with the whole NS
+        # single matrices up to m = 4096 run all iterations in one persistent
+        # kernel: it is the dominant (only) tensor kernel, credited with the
+        # MMA work it does (the SYRKs' lower triangles: "useful" FLOPs)
         dom = "fused_ns"
-        stage_flops[dom] = ns_flops(m, n)
-        kname = "ns_fused_kernel<128> (all 5 iterations, 128x128 tiles)"
+        stage_flops[dom] = NS_STEPS * (mo * (mo + 1) * no + mo * mo * (mo + 1) + 2.0 * mo * mo * no)
+        mt = (mo + 127) // 128
+        kname = ("ns_fused_kernel<128> (all 5 iterations, 128x128 tiles)" if mt * (mt + 1) // 2 <= 148
+                 else "ns_fused_pair_kernel (all 5 iterations, CTA-pair 256x256 tiles)")
     avg_dom = st[dom][0] / st[dom][1]
     achieved = stage_flops[dom] / (avg_dom * 1e-3) / 1e12
     peak = float(peaks["bf16_tflops"])

@@ -173,13 +173,16 @@ int fm_muon_apply(void* param, int dtype, const void* update, int64_t n, float d
  * 0 = automatic: a single-matrix call (fm_fused_newton_schulz, the
  *     allocation-free form) whose lower-triangle 128x128 tiles fit on the SMs
  *     runs the persistent kernel (path 4, one cooperative launch for all
- *     iterations); everything else, and every batched call, runs one launch
- *     per GEMM on CTA-pair tiles (single-CTA tiles for unbatched m <= 256),
+ *     iterations); a larger single matrix with m <= 4096 and m*n <=
+ *     4096*4608 the CTA-pair persistent kernel (path 5); everything else,
+ *     and every batched call, one launch per GEMM on CTA-pair tiles,
  * 1 = one launch per GEMM with single-CTA 128x256 tiles,
  * 2 = one launch per GEMM with CTA-pair 256x256 tiles, 3 = one persistent
  * launch for all iterations with 128x256 tiles, 4 = the same with 128x128
- * tiles.  All produce the same arithmetic (up to fp32 summation order where a
- * path splits K); the switch exists for tests and tuning.
+ * tiles, 5 = the same with CTA-pair 256x256 tiles, where the next iteration's
+ * X·Xᵀ tiles start on finished row blocks of X'.  All produce the same
+ * arithmetic (up to fp32 summation order where a path splits K); the switch
+ * exists for tests and tuning.
  * Replaces: the reference's compile-time tile dispatch, csrc/ns_gemm.cu:68-92.
  */
 int fm_set_gemm_path(int path);

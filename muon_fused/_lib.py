@@ -120,6 +120,6 @@ def launch_count() -> int:
 
 
 def set_gemm_path(path: int) -> None:
-    """0 automatic, 1 single-CTA tiles, 2 CTA-pair tiles, 3/4 persistent kernel
-    with 128x256 / 128x128 tiles (see fm_set_gemm_path)."""
+    """0 automatic, 1 single-CTA tiles, 2 CTA-pair tiles, 3/4/5 persistent
+    kernel with 128x256 / 128x128 / CTA-pair tiles (see fm_set_gemm_path)."""
     check(load().fm_set_gemm_path(int(path)), "fm_set_gemm_path")

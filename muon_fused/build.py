@@ -18,7 +18,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libfused_muon.so")
 SOURCES = ["ns_capi.cu"]
-DEPS = SOURCES + ["fm_ptx.cuh", "ns_gemm_sm100.cuh", "ns_gemm2_sm100.cuh", "ns_prep.cuh", "ns_fused_sm100.cuh",
+DEPS = SOURCES + ["fm_ptx.cuh", "ns_gemm_sm100.cuh", "ns_gemm2_sm100.cuh", "ns_prep.cuh", "ns_fused_sm100.cuh", "ns_fused2_sm100.cuh",
                   "muon_elementwise.cuh"]
 HEADER = os.path.join(os.path.dirname(HERE), "include", "fused_muon.h")
 

@@ -22,6 +22,7 @@
 #include "ns_gemm2_sm100.cuh"
 #include "ns_gemm_sm100.cuh"
 #include "ns_fused_sm100.cuh"
+#include "ns_fused2_sm100.cuh"
 #include "muon_elementwise.cuh"
 #include "ns_prep.cuh"
 
@@ -63,6 +64,12 @@ std::mutex g_mu;
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
 inline long long round_up(long long x, long long a) { return (x + a - 1) / a * a; }
+
+// Counter area of the persistent kernels in the workspace: the phase ring, then
+// 2 x T row-block counters of the CTA-pair kernel (T <= kMaxPairRows).
+constexpr int kPhaseBytes = 1024;
+constexpr int kRowdoneOffset = 16;  // ints
+constexpr int kMaxPairRows = (kPhaseBytes / 4 - kRowdoneOffset) / 2;
 
 // Optional per-stage timing for benchmarks (fm_stage_timing / fm_stage_times):
 // when enabled, each kernel launch of this thread is bracketed by CUDA events
@@ -140,6 +147,8 @@ int device_state(DeviceState** out) {
       FM_CUDA(cudaFuncSetAttribute(ns_fused_kernel<128>,
                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    FusedCfg<128>::kSmem));
+      FM_CUDA(cudaFuncSetAttribute(ns_fused_pair_kernel,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, kPairSmemBytes));
       FM_CUDA(cudaGetSymbolAddress(reinterpret_cast<void**>(&s.err_word), g_device_error));
       if (!g_encode) {
         cudaDriverEntryPointQueryResult q;
@@ -264,7 +273,8 @@ struct Workspace {
   float* partials;  // Frobenius-norm partials, kMaxPartials per matrix
   float* splitk;    // split-K fp32 partial tiles (128 KB per unit and CTA)
   int* counters;    // split-K arrival counters (two per tile: one per CTA)
-  int* phase;       // persistent kernel: phase-completion counters (kFusedSlots)
+  int* phase;       // persistent kernels: phase-completion counters (kFusedSlots),
+                    // then at kRowdoneOffset the CTA-pair kernel's row-block counters
   long long ldx, ldm, xs, ms, dsz;  // row strides and per-matrix strides (elements)
   size_t counter_bytes;
   size_t bytes;
@@ -294,7 +304,7 @@ Workspace layout(long long batch, long long m, long long n, void* base) {
   w.partials = reinterpret_cast<float*>(p + off); off += pb;
   w.splitk = reinterpret_cast<float*>(p + off); off += sb;
   w.counters = reinterpret_cast<int*>(p + off); off += w.counter_bytes;
-  w.phase = reinterpret_cast<int*>(p + off); off += 256;
+  w.phase = reinterpret_cast<int*>(p + off); off += kPhaseBytes;
   w.bytes = off;
   return w;
 }
@@ -464,11 +474,11 @@ int prep_grid(long long rows, long long cols, const DeviceState& ds) {
 // one CTA per SM, launched cooperatively so that every CTA is resident (the
 // phase-completion waits rely on it), with programmatic stream serialization
 // so its prologue overlaps the normalisation kernel.
-template <int BN>
-int run_fused(const DeviceState& ds, const Workspace& w, long long batch, long long m, long long n,
-              int steps, __nv_bfloat16* out, long long out_ld, long long out_bs, bool tall,
-              cudaStream_t st) {
-  FusedMaps maps;
+// Maps and arguments shared by both persistent kernels (tile counts are set
+// by the caller).
+int fused_setup(const DeviceState& ds, const Workspace& w, long long batch, long long m,
+                long long n, int steps, __nv_bfloat16* out, long long out_ld, long long out_bs,
+                bool tall, FusedMaps& maps, FusedArgs& f) {
   int rc;
   for (int i = 0; i < 2; ++i) {
     if ((rc = make_map(&maps.xk[i], w.X[i], batch, m, n, w.ldx, w.xs, kBK, kBM))) return rc;
@@ -489,17 +499,11 @@ int run_fused(const DeviceState& ds, const Workspace& w, long long batch, long l
                            out_bs)))
     return rc;
   if (!ok_out) maps.so_out = maps.so_x[0];  // unused: the last step stores directly
-  FusedArgs f{};
+  f = FusedArgs{};
   f.M = int(m);
   f.N = int(n);
   f.batch = int(batch);
   f.steps = steps;
-  f.t_syrk = fused_syrk_tiles<BN>(int(m));
-  f.tiles_m3 = int((m + kBM - 1) / kBM);
-  f.tiles_n3 = int((n + BN - 1) / BN);
-  const long long upi = batch * (2ll * f.t_syrk + static_cast<long long>(f.tiles_m3) * f.tiles_n3);
-  if (upi * steps > (1ll << 30)) return fail(FM_E_INVALID, "too many work units for one launch");
-  f.units_iter = int(upi);
   f.X[0] = w.X[0];
   f.X[1] = w.X[1];
   f.ldx = w.ldx;
@@ -516,7 +520,30 @@ int run_fused(const DeviceState& ds, const Workspace& w, long long batch, long l
   f.transpose_out = tall ? 1 : 0;
   f.tma_out_final = ok_out ? 1 : 0;
   f.counters = w.phase;  // zeroed by the caller before the normalisation kernels
+  f.rowdone = w.phase + kRowdoneOffset;
   f.err = ds.err_word;
+  return FM_OK;
+}
+
+int fused_units(FusedArgs& f, long long batch, int steps) {
+  const long long upi = batch * (2ll * f.t_syrk + static_cast<long long>(f.tiles_m3) * f.tiles_n3);
+  if (upi * steps > (1ll << 30)) return fail(FM_E_INVALID, "too many work units for one launch");
+  f.units_iter = int(upi);
+  return FM_OK;
+}
+
+template <int BN>
+int run_fused(const DeviceState& ds, const Workspace& w, long long batch, long long m, long long n,
+              int steps, __nv_bfloat16* out, long long out_ld, long long out_bs, bool tall,
+              cudaStream_t st) {
+  FusedMaps maps;
+  FusedArgs f;
+  if (int rc = fused_setup(ds, w, batch, m, n, steps, out, out_ld, out_bs, tall, maps, f)) return rc;
+  f.t_syrk = fused_syrk_tiles<BN>(int(m));
+  f.tiles_m3 = int((m + kBM - 1) / kBM);
+  f.tiles_n3 = int((n + BN - 1) / BN);
+  if (int rc = fused_units(f, batch, steps)) return rc;
+  const long long upi = f.units_iter;
   const int grid = int(std::min<long long>(ds.sm_count, upi * steps));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
@@ -537,6 +564,45 @@ int run_fused(const DeviceState& ds, const Workspace& w, long long batch, long l
   return FM_OK;
 }
 
+// All iterations of a batch in one persistent launch on CTA-pair tiles
+// (ns_fused2_sm100.cuh): 2-CTA clusters, one CTA per SM, cooperative.
+int run_fused_pair(const DeviceState& ds, const Workspace& w, long long batch, long long m,
+                   long long n, int steps, __nv_bfloat16* out, long long out_ld, long long out_bs,
+                   bool tall, cudaStream_t st) {
+  FusedMaps maps;
+  FusedArgs f;
+  if (int rc = fused_setup(ds, w, batch, m, n, steps, out, out_ld, out_bs, tall, maps, f)) return rc;
+  const int T = int((m + kPairBM - 1) / kPairBM);
+  if (T > kMaxPairRows) return fail(FM_E_INVALID, "matrix too large for the CTA-pair persistent kernel");
+  f.t_syrk = T * (T + 1) / 2;
+  f.tiles_m3 = T;
+  f.tiles_n3 = int((n + kPairBN - 1) / kPairBN);
+  if (int rc = fused_units(f, batch, steps)) return rc;
+  const long long units = static_cast<long long>(f.units_iter) * steps;
+  const int pairs = int(std::min<long long>(ds.sm_count / 2, units));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kPairSmemBytes;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[3];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  attr[2].id = cudaLaunchAttributeClusterDimension;
+  attr[2].val.clusterDim.x = 2;
+  attr[2].val.clusterDim.y = 1;
+  attr[2].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 3;
+  const long long tm = timer_begin(4, st);
+  FM_CUDA(cudaLaunchKernelEx(&cfg, ns_fused_pair_kernel, maps, f));
+  note_launch();
+  timer_end(tm, st);
+  return FM_OK;
+}
+
 // Automatic choice of the persistent kernel (128 x 128 tiles): when one wave
 // of SMs covers a whole SYRK phase, i.e. the batch's lower-triangle 128 x 128
 // tiles fit on the SMs.  Then every phase is latency-bound (one tile per SM)
@@ -547,6 +613,16 @@ int run_fused(const DeviceState& ds, const Workspace& w, long long batch, long l
 bool use_persistent(long long batch, long long m, const DeviceState& ds) {
   const long long mt = (m + kBM - 1) / kBM;
   return batch * (mt * (mt + 1) / 2) <= ds.sm_count;
+}
+
+// Automatic choice of the CTA-pair persistent kernel: a single matrix past
+// the range above whose X (and A, B) stay in L2 — its B·X phase walks row
+// blocks, which re-reads X once per row block.  Measured (power-capped, 30
+// calls): 3072² 607 vs 636-678 µs, (3584, 4608) 1033-1040 vs 1098-1220 µs,
+// 4096² 1235-1253 vs 1255 µs against one launch per GEMM; (4096, 6144) was
+// 3% slower, so the bound stops below it.
+bool use_persistent_pairs(long long batch, long long m, long long n) {
+  return batch == 1 && m <= 4096 && m * n <= 4096ll * 4608ll;
 }
 
 // Full Newton-Schulz over a batch of same-shape matrices (batch = 1 for the
@@ -578,8 +654,14 @@ int ns_run(const void* G, int dtype, long long batch, long long rows, long long 
     return fail(FM_E_WORKSPACE, "workspace too small: need %zu bytes, got %llu", w.bytes,
                 (unsigned long long)workspace_bytes);
   int path = g_gemm_path.load(std::memory_order_relaxed);
-  if (path == 0 && auto_persistent && use_persistent(batch, m, *ds)) path = 4;
-  const bool persistent = path == 3 || path == 4;
+  if (path == 0 && auto_persistent) {
+    if (use_persistent(batch, m, *ds)) {
+      path = 4;
+    } else if (use_persistent_pairs(batch, m, n)) {
+      path = 5;
+    }
+  }
+  const bool persistent = path == 3 || path == 4 || path == 5;
   const NsPlan P = plan_ns(batch, m, n, persistent ? 1 : path);
   auto* o = static_cast<__nv_bfloat16*>(out);
 
@@ -588,7 +670,7 @@ int ns_run(const void* G, int dtype, long long batch, long long rows, long long 
   // Zero the counters a launch relies on before the normalisation kernels,
   // so the kernels that follow them keep their programmatic overlap.
   if (persistent && steps > 0) {
-    FM_CUDA(cudaMemsetAsync(w.phase, 0, kFusedSlots * sizeof(int), st));
+    FM_CUDA(cudaMemsetAsync(w.phase, 0, kPhaseBytes, st));
   } else if (P.split_slots > 0 && steps > 0) {
     FM_CUDA(cudaMemsetAsync(w.counters, 0, w.counter_bytes, st));
   }
@@ -618,6 +700,7 @@ int ns_run(const void* G, int dtype, long long batch, long long rows, long long 
   timer_end(tm, st);
   if (persistent) {
     const long long out_ld = tall ? m : n;
+    if (path == 5) return run_fused_pair(*ds, w, batch, m, n, steps, o, out_ld, bs_out, tall, st);
     return path == 3 ? run_fused<256>(*ds, w, batch, m, n, steps, o, out_ld, bs_out, tall, st)
                      : run_fused<128>(*ds, w, batch, m, n, steps, o, out_ld, bs_out, tall, st);
   }
@@ -810,7 +893,7 @@ int fm_muon_apply(void* param, int dtype, const void* update, int64_t n, float d
 }
 
 int fm_set_gemm_path(int path) {
-  if (path < 0 || path > 4) return fail(FM_E_INVALID, "gemm path must be in [0, 4], got %d", path);
+  if (path < 0 || path > 5) return fail(FM_E_INVALID, "gemm path must be in [0, 5], got %d", path);
   g_gemm_path.store(path);
   return FM_OK;
 }

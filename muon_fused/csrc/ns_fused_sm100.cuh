@@ -80,6 +80,8 @@ struct FusedArgs {
   int transpose_out;
   int tma_out_final;   // 1: the destination has 16-byte aligned rows (so_out valid)
   int* counters;       // kFusedSlots phase counters, zero at launch
+  int* rowdone;        // CTA-pair kernel: 2 x tiles_m3 row-block counters of the
+                       // B·X phases (iteration parity), zero at launch
   unsigned* err;
 };
 

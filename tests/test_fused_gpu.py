@@ -85,3 +85,32 @@ def test_fused_repeated_calls_reuse_workspace(cuda_lib):
     outs = _with_path(3, lambda: [fused_newton_schulz(G, 5, ws) for _ in range(4)])
     for o in outs[1:]:
         assert torch.equal(o, outs[0])
+
+
+@pytest.mark.parametrize("shape", [(2560, 2560), (3072, 4096), (4096, 4096), (1536, 2048),
+                                   (2304, 3000), (4096, 2560), (300, 700)])
+def test_fused_pair_bit_identical(cuda_lib, shape):
+    """The CTA-pair persistent kernel (path 5: 256x256 tiles, the next
+    iteration's X·Xᵀ tiles start on finished row blocks of X') equals the
+    single-CTA per-GEMM path bit for bit: same per-element accumulation, and
+    neither splits K.  Square, wide, tall (transposed output), ragged."""
+    from muon_fused import _lib, fused_newton_schulz
+
+    G = torch.randn(*shape, generator=torch.Generator().manual_seed(sum(shape) + 1)).bfloat16()
+    Gd = G.to(DEV)
+    want = _with_path(1, lambda: fused_newton_schulz(Gd, 5))
+    got = _with_path(5, lambda: fused_newton_schulz(Gd, 5))
+    assert torch.equal(got, want), shape
+    assert _lib.device_error() == 0
+
+
+@pytest.mark.parametrize("steps", [1, 2, 7])
+def test_fused_pair_step_counts_and_batch(cuda_lib, steps):
+    from muon_fused import _fused_muon_C as _C
+
+    G = torch.randn(3, 1280, 2304, generator=torch.Generator().manual_seed(steps)).bfloat16()
+    Gd = G.to(DEV)
+    got = _with_path(5, lambda: _C.fused_newton_schulz_batched(Gd, steps))
+    for i in range(3):
+        want = _with_path(1, lambda: _C.fused_newton_schulz(Gd[i], steps))
+        assert torch.equal(got[i], want), i
