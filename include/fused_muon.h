@@ -209,6 +209,19 @@ int fm_stage_times(float* ms, int* counts);
  */
 int fm_launch_count(uint64_t* count);
 
+#ifdef FM_TRACE
+/*
+ * Development builds only (compiled with -DFM_TRACE; the shipped library does
+ * not export these).  Copy the kernels' %globaltimer timelines to host memory
+ * after synchronising the device: fm_trace_read the CTA-pair GEMMs' (3 modes x
+ * 128 pairs x 40 u64), fm_fused_trace_read the persistent kernel's
+ * (160 CTAs x 64 units x 4 u64).
+ * Replaces: nothing (instrumentation).
+ */
+int fm_trace_read(void* host);
+int fm_fused_trace_read(void* host);
+#endif
+
 #ifdef __cplusplus
 }
 #endif

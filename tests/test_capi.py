@@ -13,7 +13,9 @@ HEADER = os.path.join(ROOT, "include", "fused_muon.h")
 
 
 def declared_symbols():
-    text = open(HEADER).read()
+    """Entry points of the shipped library: declarations outside the
+    development-only `#ifdef FM_TRACE` block."""
+    text = re.sub(r"#ifdef FM_TRACE.*?#endif", "", open(HEADER).read(), flags=re.S)
     return sorted(set(re.findall(r"^\w[\w\s\*]*?\b(fm_\w+)\s*\(", text, flags=re.M)))
 
 
