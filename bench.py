@@ -458,7 +458,8 @@ def bench_muon(args, world, rank, peaks, peak_src):
                              device=dev, dtype=torch.bfloat16) * 1e-3
         params.append(p)
     opt = FusedMuon([{"params": params, "use_muon": True}], lr=0.02, momentum=0.95, nesterov=True,
-                    ns_steps=NS_STEPS, collective=args.collective)
+                    ns_steps=NS_STEPS, collective=args.collective,
+                    bucket_bytes=args.bucket_mib << 20)
     for _ in range(args.warmup):
         opt.step()
     torch.cuda.synchronize()
@@ -557,6 +558,7 @@ def bench_muon(args, world, rank, peaks, peak_src):
                    "stream during the previous step; rank 0's bytes"}
     extra = {"matrices": len(shapes)}
     if world > 1:
+        extra["bucket_mib"] = args.bucket_mib
         extra["ranks_agree"], extra["owner_check"] = verify_sharded(opt, params, shapes, owner,
                                                                     world, rank)
     return {"ms": ms, "flops": flops, "roofline": roofline, "clocks": clk.summary(), "e2e": e2e,
@@ -817,6 +819,9 @@ def main():
     ap.add_argument("--collective", choices=["nccl", "param_gather"], default="param_gather",
                     help="sharded-step exchange: all-gather of the updates + apply on every "
                          "rank, or owner apply + in-place all-gather of the parameters")
+    ap.add_argument("--bucket-mib", type=int, default=256,
+                    help="sharded step: per-rank all-gather bucket size in MiB (FusedMuon's "
+                         "bucket_bytes)")
     ap.add_argument("--shape", type=int, nargs=2, default=list(SHAPE_NS),
                     help="ns workload matrix shape (default: the headline 4096 4096)")
     ap.add_argument("--quick", action="store_true",
